@@ -1,0 +1,344 @@
+#!/usr/bin/env python3
+"""Benchmark: NVFP4 -> HiF4 conversion throughput (Gelem/s) on B200.
+
+Workload (one step): one 16384 x 16384 NVFP4 tensor (N(0, 0.02) bf16,
+E2M1 codes + E4M3 per-16 scales + fp32 tensor scale), converted by the
+fused kernel (decode -> 64-point rotation -> searched HiF4 encode -> packed
+HiF4), then the HiF4 -> bf16 decode round trip.  Inputs and outputs
+(~0.84 GB) exceed the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hif4x|reference]
+
+For N > 1 launch with torch.distributed.run; every rank converts its own
+tensor (weak scaling, no data-path collective).  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hif4-contest_b200"))
+
+ROWS = COLS = 16384
+METRIC = "NVFP4->HiF4 Gelem/s (codec: decode, rot64, searched encode, HiF4 decode round trip)"
+ALG_BYTES_PER_ELEM = 1.125          # packed NVFP4 in (0.5625) + packed HiF4 out (0.5625)
+ROUNDTRIP_BYTES_PER_ELEM = 3.6875   # + HiF4 re-read (0.5625) + bf16 write (2)
+CPU_SAMPLE_ROWS = 4096
+
+
+def workload_config():
+    return {"workload": "codec config: 16384x16384 NVFP4 -> HiF4 (decode, rot64, 6-candidate searched "
+                        "encode, packed HiF4) + HiF4->bf16 round trip",
+            "rows": ROWS, "cols": COLS, "elements_per_step_per_gpu": ROWS * COLS,
+            "l2_policy": "working set 0.84 GB per step > 126 MB L2; no flush",
+            "parallelism": "replicas per GPU (weak scaling, no collective)"}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl" if os.environ.get("HIF4X_BENCH_BACKEND") != "gloo" else "gloo",
+                                timeout=datetime.timedelta(seconds=120))
+        return dist.get_rank(), ws, int(os.environ.get("LOCAL_RANK", "0"))
+    return 0, 1, 0
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples at 50 ms while running."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "50"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float):
+        def parse(s):
+            f = [x.strip() for x in s.split(",")]
+            try:
+                return {"sm": float(f[0]), "max": float(f[1]), "hw": f[4], "hwt": f[5], "swt": f[6], "pc": f[7]}
+            except (ValueError, IndexError):
+                return None
+        inside = [parse(s) for (t, s) in self.samples if t0 <= t <= t1]
+        inside = [p for p in inside if p]
+        window = "timed region"
+        if not inside:  # short timed region: nearest samples around it
+            near = sorted(self.samples, key=lambda ts: min(abs(ts[0] - t0), abs(ts[0] - t1)))[:5]
+            inside = [p for p in (parse(s) for _, s in near) if p]
+            window = "nearest samples (timed region shorter than the sampling period)"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = set()
+        for p in inside:
+            for k, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                            ("pc", "sw_power_cap")):
+                if p[k].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(p["sm"] for p in inside), "sm_max_mhz": inside[0]["max"],
+                "reasons": sorted(reasons), "samples": len(inside), "window": window}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "convert_c1_16384.json")) as f:
+            d = json.load(f)
+        return d.get("dram_bytes_per_launch_full_size")
+    except (OSError, ValueError):
+        return None
+
+
+def cpu_oracle_sample(codes, e4m3, s_dec, rows):
+    """The oracle chain on the first `rows` rows; returns (elements/s, threads, seconds)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # CPU baseline leg only
+    n = os.cpu_count() or 1
+    oracle.set_threads(n)
+    c = codes[:rows].cpu().numpy()
+    e = e4m3[:rows].cpu().numpy()
+    oracle.codec_roundtrip(c[:8], e[:8], s_dec)  # load + warm
+    t = time.perf_counter()
+    oracle.codec_roundtrip(c, e, s_dec)
+    dt = time.perf_counter() - t
+    return rows * COLS / dt, n, dt
+
+
+def run_reference(args, rank, ws):
+    """Reference arm: the reference's CPU path (its restatement in oracle/)
+    on the host cores, on bounded samples of the same workload."""
+    if rank != 0:
+        return
+    import torch
+
+    from hif4x import synth
+    sample_rows = 1024
+    x = synth.codec_c1(1000, sample_rows, COLS)
+    codes, e4m3, s_dec = synth.quantize_nvfp4(x)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    n = os.cpu_count() or 1
+    oracle.set_threads(n)
+    c, e = codes.numpy(), e4m3.numpy()
+    for _ in range(args.warmup):
+        oracle.codec_roundtrip(c[:64], e[:64], s_dec)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.codec_roundtrip(c, e, s_dec)
+    dt = (time.perf_counter() - t) / max(args.steps, 1)
+    v = sample_rows * COLS / dt / 1e9
+    sample = f"{sample_rows}x{COLS} rows of the workload per step (oracle port of the reference codec)"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "Gelem/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(),
+        "cpu_baseline": {"value": v, "unit": "Gelem/s", "cores": n, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    del torch
+
+
+def run_gpu(args, rank, ws, local_rank):
+    import torch
+
+    from hif4x import _lib as L
+    from hif4x import codec, synth
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+
+    x = synth.codec_c1(1000 + rank, ROWS, COLS, device=dev)
+    codes, e4m3, s_dec = synth.quantize_nvfp4(x)
+    del x
+    torch.cuda.empty_cache()
+    meta = torch.empty(ROWS, COLS // 64, dtype=torch.int32, device=dev)
+    hcodes = torch.empty(ROWS, COLS // 2, dtype=torch.uint8, device=dev)
+    rt = torch.empty(ROWS, COLS, dtype=torch.bfloat16, device=dev)
+    signs = codec.rot_signs(COLS // 64, dev)
+    d = L.ConvertDesc()
+    d.rows, d.cols, d.src_kind, d.s_dec = ROWS, COLS, L.SRC_NVFP4_PACKED, s_dec
+    d.src, d.src_scale, d.rot_signs, d.encode_mode = codes.data_ptr(), e4m3.data_ptr(), signs.data_ptr(), L.ENC_SEARCH
+    d.meta, d.codes = meta.data_ptr(), hcodes.data_ptr()
+    stream = torch.cuda.current_stream(dev)
+    sp = L.vp(stream.cuda_stream)
+    dref = L.ctypes.byref(d)
+
+    def step(ev_a=None, ev_b=None):
+        if ev_a is not None:
+            ev_a.record(stream)
+        L.call("hif4x_convert", dref, sp)
+        if ev_b is not None:
+            ev_b.record(stream)
+        L.call("hif4x_decode_packed", L.ptr(meta), L.ptr(hcodes), ROWS, COLS, L.ptr(rt), L.DT_BF16, sp)
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = int(vis.split(",")[local_rank]) if vis and vis.split(",")[local_rank].strip().isdigit() else local_rank
+    clk = ClockSampler(phys)
+    clk.start()
+    time.sleep(0.3)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    K = args.steps
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    w0 = time.time()
+    t_start.record(stream)
+    for k in range(K):
+        step(*evs[k])
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    w1 = time.time()
+    barrier()
+    ms = t_start.elapsed_time(t_end) / K
+    k_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    if dist is not None:
+        t = torch.tensor([ms, k_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, k_ms = float(t[0]), float(t[1])
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dist)
+    clk.stop()
+    if rank != 0:
+        return
+    elems = ROWS * COLS
+    value = ws * elems / (ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    achieved = elems * ALG_BYTES_PER_ELEM / (k_ms * 1e-3) / 1e9
+    traffic = ncu_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": ws, "steps": K, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(),
+        "codec_gbs_roundtrip": elems * ROUNDTRIP_BYTES_PER_ELEM / (ms * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "hif4x convert_kernel (decode+rot64+searched encode)",
+                     "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "kernel_ms": k_ms,
+                     "alg_bytes_per_launch": elems * ALG_BYTES_PER_ELEM},
+        "gpu_launches": 2 * K,
+        "clocks": clk.summary(w0, w1),
+    }
+    if e2e is not None:
+        e2e_ms, launches_e2e, h2d, d2h = e2e
+        line["e2e"] = {"value": ws * elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "gpu_launches": launches_e2e}
+    if ws == 1 and not args.no_cpu_baseline:
+        v, n, dt = cpu_oracle_sample(codes, e4m3, s_dec, CPU_SAMPLE_ROWS)
+        line["cpu_baseline"] = {"value": v / 1e9, "unit": "Gelem/s", "cores": n, "kind": "port",
+                                "sample": f"first {CPU_SAMPLE_ROWS} of {ROWS} rows of the same tensor "
+                                          f"({dt:.1f} s, oracle C port of the reference codec, OpenMP)"}
+    print(json.dumps(line), flush=True)
+
+
+def e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dist):
+    """The same conversion through the host-buffer API: pinned host input,
+    H2D, kernels, D2H of the packed HiF4 result, all inside the timed region."""
+    import torch
+
+    from hif4x.api import PackedConverter
+    codes_h = codes.cpu().pin_memory()
+    e4m3_h = e4m3.cpu().pin_memory()
+    meta_h = torch.empty(ROWS, COLS // 64, dtype=torch.int32).pin_memory()
+    hcodes_h = torch.empty(ROWS, COLS // 2, dtype=torch.uint8).pin_memory()
+    conv = PackedConverter(ROWS, COLS, device=dev, chunk_rows=2048, rotate=True, roundtrip=True)
+    for _ in range(max(2, args.warmup)):
+        conv(codes_h, e4m3_h, s_dec, meta_h, hcodes_h)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    launches_e2e = 0
+    for _ in range(K):
+        launches_e2e += conv(codes_h, e4m3_h, s_dec, meta_h, hcodes_h)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / K
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    # the e2e result must match the device-resident run
+    assert torch.equal(meta_h.to(dev), meta) and torch.equal(hcodes_h.to(dev), hcodes)
+    return e2e_ms, launches_e2e, int(codes_h.numel() + e4m3_h.numel()), int(meta_h.numel() * 4 + hcodes_h.numel())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="hif4x", choices=["hif4x", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        # rank 0 alone times the CPU reference; the other ranks exit at once
+        run_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        return
+    rank, ws, local_rank = dist_init()
+    try:
+        run_gpu(args, rank, ws, local_rank)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

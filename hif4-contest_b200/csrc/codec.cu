@@ -1,0 +1,862 @@
+// codec.cu -- NVFP4 decode, 64-point block rotation and HiF4 encode/decode.
+//
+// One thread owns one 64-element HiF4 group end to end (decode -> smoothing
+// -> rotation -> encode -> stores), so the tensor is read once and every
+// reduction of the reference (amax, quad/sub-block/group error sums) is a
+// thread-local sequential loop in exactly the reference's order.  The
+// group's |x| is staged in shared memory, transposed (element k of thread t
+// at k*blockDim + t), so the encode can loop over sub-blocks at run time
+// without bank conflicts.
+//
+// Bit-exactness with the reference's torch CPU arithmetic:
+//  * every rounding step is an explicit __f*_rn intrinsic (no contraction);
+//  * floor(log2(t)) uses a table of torch's thresholds (log2_floor_table.h);
+//  * |x| / unit with unit = sig * 2^E is computed by Markstein's correction
+//    (q0 = |x|*y, r = fma(-q0, u, |x|), q = fma(r, y, q0), y = RN(1/u)),
+//    which returns the correctly rounded quotient for sig in {1.25, 1.5,
+//    1.75} (checked exhaustively over all fp32 significands on the CPU);
+//  * round-half-even of q*4*2^-m in [0, 56] is fma(q, 2^(2-m), 1.5*2^23) -
+//    1.5*2^23, exact in that range;
+//  * the 64-point rotation is summed in the reference's sequential order,
+//    or by a fast Walsh-Hadamard transform when every partial sum is
+//    provably exact (then every summation order gives the same result).
+#include "common.cuh"
+#include "log2_floor_table.h"
+
+namespace hif4x {
+
+constexpr int kConvThreads = 128;
+
+struct ConvParams {
+  int64_t ngroups, nb;
+  int src_kind, src_dtype, scale_dtype;
+  float s_dec;
+  const void *src;
+  const void *src_scale;
+  const float *smooth;
+  int smooth_mode;
+  const uint64_t *rot_signs;
+  int encode_mode;
+  float *out_x;
+  float *sf, *lv2, *lv3, *sign, *mant;
+  uint32_t *meta;
+  uint8_t *codes;
+  void *deq;
+  int deq_dtype;
+  float *unit;
+};
+
+// floor(torch.log2(t)) for finite t > 0.
+__device__ __forceinline__ int floor_log2_torch(float t) {
+  const uint32_t b = __float_as_uint(t);
+  int e = (int)(b >> 23) - 127;
+  if ((b >> 23) == 0) e = (31 - __clz((int)b)) - 149;
+  e = min(e, HIF4X_LOG2_EMAX);
+  return e + (b >= HIF4X_LOG2_UP[e - HIF4X_LOG2_EMIN] ? 1 : 0);
+}
+
+// ---------------------------------------------------------------- loading
+__device__ __forceinline__ void load_group(const ConvParams &p, int64_t g, float (&x)[64]) {
+  if (p.src_kind == HIF4X_SRC_NVFP4_PACKED) {
+    const uint4 *c4 = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.src) + g * 32);
+    const uint4 v0 = __ldcs(c4), v1 = __ldcs(c4 + 1);
+    const uint32_t sc = __ldcs(reinterpret_cast<const unsigned int *>(p.src_scale) + g);
+    float s[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) s[k] = __fmul_rn(e4m3_to_f32((sc >> (8 * k)) & 0xffu), p.s_dec);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+      for (int n = 0; n < 8; n++)
+        x[8 * j + n] = bf16_round(__fmul_rn(e2m1_to_f32((w[j] >> (4 * n)) & 15u), s[j >> 1]));
+    return;
+  }
+  if (p.src_kind == HIF4X_SRC_NVFP4_PAIR) {
+    float s[4];
+    if (p.scale_dtype == HIF4X_DT_F32) {
+      const float4 sv = __ldg(reinterpret_cast<const float4 *>(p.src_scale) + g);
+      s[0] = sv.x; s[1] = sv.y; s[2] = sv.z; s[3] = sv.w;
+    } else {
+      const uint2 sv = __ldg(reinterpret_cast<const uint2 *>(p.src_scale) + g);
+      s[0] = __uint_as_float(sv.x << 16); s[1] = __uint_as_float(sv.x & 0xffff0000u);
+      s[2] = __uint_as_float(sv.y << 16); s[3] = __uint_as_float(sv.y & 0xffff0000u);
+    }
+    if (p.src_dtype == HIF4X_DT_F32) {
+      const float4 *c4 = reinterpret_cast<const float4 *>(p.src) + g * 16;
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const float4 v = __ldcs(c4 + j);
+        x[4 * j + 0] = bf16_round(__fmul_rn(v.x, s[j >> 2]));
+        x[4 * j + 1] = bf16_round(__fmul_rn(v.y, s[j >> 2]));
+        x[4 * j + 2] = bf16_round(__fmul_rn(v.z, s[j >> 2]));
+        x[4 * j + 3] = bf16_round(__fmul_rn(v.w, s[j >> 2]));
+      }
+    } else {
+      const uint4 *c4 = reinterpret_cast<const uint4 *>(p.src) + g * 8;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const uint4 v = __ldcs(c4 + j);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int n = 0; n < 4; n++) {
+          x[8 * j + 2 * n] = bf16_round(__fmul_rn(__uint_as_float(w[n] << 16), s[j >> 1]));
+          x[8 * j + 2 * n + 1] = bf16_round(__fmul_rn(__uint_as_float(w[n] & 0xffff0000u), s[j >> 1]));
+        }
+      }
+    }
+    return;
+  }
+  // plain values
+  if (p.src_dtype == HIF4X_DT_F32) {
+    const float4 *c4 = reinterpret_cast<const float4 *>(p.src) + g * 16;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const float4 v = __ldg(c4 + j);
+      x[4 * j] = v.x; x[4 * j + 1] = v.y; x[4 * j + 2] = v.z; x[4 * j + 3] = v.w;
+    }
+  } else {
+    const uint4 *c4 = reinterpret_cast<const uint4 *>(p.src) + g * 8;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint4 v = __ldg(c4 + j);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int n = 0; n < 4; n++) {
+        x[8 * j + 2 * n] = __uint_as_float(w[n] << 16);
+        x[8 * j + 2 * n + 1] = __uint_as_float(w[n] & 0xffff0000u);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- rotation
+// out[e] = sum_{d=0..63} x[d] * (H64[d][e] / 8 * sign_e), summed d = 0..63
+// from +0 as torch's CPU einsum does (solution.py:243-245).
+// `stage` is the thread's transposed shared-memory column (stride `st`).
+__device__ __forceinline__ void rot64_exact(float (&x)[64], uint64_t sgn, float *stage, int st) {
+  // Exactness test: all x are multiples of 2^L; if sum|x| < 2^(L+23) every
+  // partial sum of any order is representable, so the FWHT equals the
+  // sequential sum bit for bit.
+  int L = 1 << 20;
+  float S = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 64; k++) {
+    const uint32_t b = __float_as_uint(x[k]);
+    const int ef = (int)((b >> 23) & 255u);
+    const uint32_t m = (b & 0x7fffffu) | 0x800000u;
+    const int lsb = (b & 0x7fffffffu) == 0u ? (1 << 20) : (ef == 0 ? -(1 << 20) : ef - 150 + (__ffs((int)m) - 1));
+    L = min(L, lsb);
+    S = __fadd_rn(S, fabsf(x[k]));
+  }
+  const bool fast = (L >= -120) && (L + 23 > 127 || S < exp2i(L + 23));
+  if (fast) {
+#pragma unroll
+    for (int lg = 0; lg < 6; lg++) {
+#pragma unroll
+      for (int j = 0; j < 64; j++) {
+        const int h = 1 << lg;
+        if ((j & h) == 0) {
+          const float a = x[j], b = x[j + h];
+          x[j] = __fadd_rn(a, b);
+          x[j + h] = __fsub_rn(a, b);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 64; e++) x[e] = __fmul_rn(x[e], ((sgn >> e) & 1ull) ? -0.125f : 0.125f);
+    return;
+  }
+  // Sequential path (wide dynamic range): the reference's order exactly.
+  // Walsh masks: bit d of W_b is bit b of d.
+  const uint64_t W[6] = {0xAAAAAAAAAAAAAAAAull, 0xCCCCCCCCCCCCCCCCull, 0xF0F0F0F0F0F0F0F0ull,
+                         0xFF00FF00FF00FF00ull, 0xFFFF0000FFFF0000ull, 0xFFFFFFFF00000000ull};
+#pragma unroll 1
+  for (int e = 0; e < 64; e++) {
+    uint64_t par = 0;  // bit d = parity(d & e)
+#pragma unroll
+    for (int b = 0; b < 6; b++)
+      if ((e >> b) & 1) par ^= W[b];
+    const float de = ((sgn >> e) & 1ull) ? -1.0f : 1.0f;
+    float acc = 0.0f;
+#pragma unroll
+    for (int d = 0; d < 64; d++) {
+      const float rm = __fmul_rn(((par >> d) & 1ull) ? -0.125f : 0.125f, de);
+      acc = __fadd_rn(acc, __fmul_rn(x[d], rm));
+    }
+    stage[e * st] = acc;
+  }
+#pragma unroll
+  for (int e = 0; e < 64; e++) x[e] = stage[e * st];
+}
+
+// ---------------------------------------------------------------- encode
+// Result of an encode: sf, lv bits (bit i = lv2 of sub-block i is 2, bit
+// 8+j = lv3 of quad j is 2), and how to rebuild each element's unit.
+struct Enc {
+  float sf;
+  uint32_t bits;
+};
+
+// Searched encode, fast path: every candidate scale is inside the E6M2
+// range, so the 6 candidates x 3 lv units collapse onto 14 distinct units
+// sig * 2^(e0+m) (sig in {1, 1.25, 1.5, 1.75}; m in 0..3 for sig 1, 1.25
+// and 0..2 for 1.5, 1.75), each evaluated once per element.
+__device__ __forceinline__ Enc search_fast(const float *stage, int st, int e0) {
+  const float p2 = exp2i(e0);
+  const float u[4] = {p2, __fmul_rn(p2, 1.25f), __fmul_rn(p2, 1.5f), __fmul_rn(p2, 1.75f)};
+  const float y[4] = {exp2i(-e0), __fdiv_rn(1.0f, u[1]), __fdiv_rn(1.0f, u[2]), __fdiv_rn(1.0f, u[3])};
+  // quarter units uq[s][m] = u[s] * 2^(m-2)
+  float err[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  uint32_t bits[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll 1
+  for (int i = 0; i < 8; i++) {
+    float Q[2][14];
+#pragma unroll
+    for (int qd = 0; qd < 2; qd++) {
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const float a = stage[(8 * i + 4 * qd + kk) * st];
+        float q[4];
+        q[0] = __fmul_rn(a, y[0]);  // exact: y[0] is a power of two
+#pragma unroll
+        for (int s = 1; s < 4; s++) {
+          const float q0 = __fmul_rn(a, y[s]);
+          const float r = __fmaf_rn(-q0, u[s], a);
+          q[s] = __fmaf_rn(r, y[s], q0);
+        }
+#pragma unroll
+        for (int idx = 0; idx < 14; idx++) {
+          // unit idx = sig SU * 2^(e0 + MU); SU = 0,0,0,0,1,1,1,1,2,2,2,3,3,3
+          const int s = idx < 4 ? 0 : idx < 8 ? 1 : idx < 11 ? 2 : 3;
+          const int m = idx < 8 ? (idx & 3) : (idx < 11 ? idx - 8 : idx - 11);
+          const float qs = (m == 0) ? 4.0f : (m == 1) ? 2.0f : (m == 2) ? 1.0f : 0.5f;
+          const float uq = __fmul_rn(u[s], (m == 0) ? 0.25f : (m == 1) ? 0.5f : (m == 2) ? 1.0f : 2.0f);
+          const float t = fminf(__fmaf_rn(q[s], qs, kMagic), kMagic + 7.0f);
+          const float mm = __fsub_rn(t, kMagic);
+          const float d = __fmaf_rn(mm, uq, -a);
+          const float e = __fmul_rn(d, d);
+          Q[qd][idx] = kk ? __fadd_rn(Q[qd][idx], e) : e;
+        }
+      }
+    }
+    const int BASE[6] = {0, 4, 8, 11, 1, 5};
+#pragma unroll
+    for (int c = 0; c < 6; c++) {
+      const int b0 = BASE[c];
+      const bool t0 = Q[0][b0] <= Q[0][b0 + 1];
+      const bool t1 = Q[1][b0] <= Q[1][b0 + 1];
+      const float e2a = __fadd_rn(t0 ? Q[0][b0] : Q[0][b0 + 1], t1 ? Q[1][b0] : Q[1][b0 + 1]);
+      const bool s0 = Q[0][b0 + 1] <= Q[0][b0 + 2];
+      const bool s1 = Q[1][b0 + 1] <= Q[1][b0 + 2];
+      const float e2b = __fadd_rn(s0 ? Q[0][b0 + 1] : Q[0][b0 + 2], s1 ? Q[1][b0 + 1] : Q[1][b0 + 2]);
+      const bool take2 = e2b < e2a;
+      const float best = take2 ? e2b : e2a;
+      const uint32_t l3 = take2 ? ((s0 ? 0u : 1u) | (s1 ? 0u : 2u)) : ((t0 ? 0u : 1u) | (t1 ? 0u : 2u));
+      bits[c] |= ((take2 ? 1u : 0u) << i) | (l3 << (8 + 2 * i));
+      err[c] = __fadd_rn(err[c], best);
+    }
+  }
+  int cb = 0;
+  float eb = err[0];
+#pragma unroll
+  for (int c = 1; c < 6; c++)
+    if (err[c] < eb) { eb = err[c]; cb = c; }
+  const int SIGI[6] = {0, 1, 2, 3, 0, 1};
+  float ub = u[0];
+  uint32_t bb = bits[0];
+#pragma unroll
+  for (int c = 1; c < 6; c++)
+    if (cb == c) { ub = u[SIGI[c]]; bb = bits[c]; }
+  Enc r;
+  r.sf = __fmul_rn(ub, cb >= 4 ? 2.0f : 1.0f);
+  r.bits = bb;
+  return r;
+}
+
+// Literal restatement of _quant_chunk for groups whose candidate scales hit
+// the E6M2 clamps (all-zero, tiny or huge groups).  IEEE divisions, rintf.
+__device__ __forceinline__ float sq_err_ref(float a, float unit) {
+  float q = __fmul_rn(__fdiv_rn(a, unit), 4.0f);
+  q = clampf(__fmul_rn(rintf(q), 0.25f), 0.0f, 1.75f);
+  const float d = __fsub_rn(__fmul_rn(q, unit), a);
+  return __fmul_rn(d, d);
+}
+
+__device__ __noinline__ Enc search_generic(const float *stage, int st, int e0) {
+  const int K[6] = {0, 0, 0, 0, 1, 1};
+  const float SIG[6] = {1.0f, 1.25f, 1.5f, 1.75f, 1.0f, 1.25f};
+  float eb = 0.0f, sfb = 0.0f;
+  uint32_t bb = 0;
+#pragma unroll 1
+  for (int c = 0; c < 6; c++) {
+    const float sf = clampf(__fmul_rn(exp2i(e0 + K[c]), SIG[c]), kSfMin, kSfMax);
+    float err = 0.0f;
+    uint32_t bits = 0;
+#pragma unroll 1
+    for (int i = 0; i < 8; i++) {
+      float e3[2][2][2];  // [lv2][lv3][quad]
+#pragma unroll
+      for (int l2 = 0; l2 < 2; l2++)
+#pragma unroll
+        for (int l3 = 0; l3 < 2; l3++) {
+          const float unit = __fmul_rn(__fmul_rn(sf, l2 ? 2.0f : 1.0f), l3 ? 2.0f : 1.0f);
+#pragma unroll
+          for (int qd = 0; qd < 2; qd++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) s = __fadd_rn(s, sq_err_ref(stage[(8 * i + 4 * qd + kk) * st], unit));
+            e3[l2][l3][qd] = s;
+          }
+        }
+      float e2[2];
+      uint32_t l3b[2];
+#pragma unroll
+      for (int l2 = 0; l2 < 2; l2++) {
+        const bool t0 = e3[l2][0][0] <= e3[l2][1][0];
+        const bool t1 = e3[l2][0][1] <= e3[l2][1][1];
+        e2[l2] = __fadd_rn(t0 ? e3[l2][0][0] : e3[l2][1][0], t1 ? e3[l2][0][1] : e3[l2][1][1]);
+        l3b[l2] = (t0 ? 0u : 1u) | (t1 ? 0u : 2u);
+      }
+      const bool take2 = e2[1] < e2[0];
+      bits |= ((take2 ? 1u : 0u) << i) | ((take2 ? l3b[1] : l3b[0]) << (8 + 2 * i));
+      err = __fadd_rn(err, take2 ? e2[1] : e2[0]);
+    }
+    if (c == 0 || err < eb) { eb = err; sfb = sf; bb = bits; }
+  }
+  Enc r;
+  r.sf = sfb;
+  r.bits = bb;
+  return r;
+}
+
+// _quant_weight_fast (solution.py:787-823): greedy lv tree, anchor exponent,
+// four significands; the 64 errors are summed left to right.
+__device__ __noinline__ Enc encode_fast(const float *stage, int st, float amax) {
+  float a4[16], a8[8];
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    float m = stage[(4 * j) * st];
+#pragma unroll
+    for (int k = 1; k < 4; k++) m = fmaxf(m, stage[(4 * j + k) * st]);
+    a4[j] = m;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) a8[i] = fmaxf(a4[2 * i], a4[2 * i + 1]);
+  const float t = fmaxf(__fdiv_rn(amax, 7.0f), 1e-38f);
+  const int e0 = floor_log2_torch(t);
+  const float SIG[4] = {1.0f, 1.25f, 1.5f, 1.75f};
+  float eb = 0.0f, sfb = 0.0f;
+#pragma unroll 1
+  for (int c = 0; c < 4; c++) {
+    const float sf = clampf(__fmul_rn(exp2i(e0), SIG[c]), kSfMin, kSfMax);
+    float err = 0.0f;
+#pragma unroll 1
+    for (int i = 0; i < 8; i++) {
+      const float l2 = (__fdiv_rn(a8[i], sf) > 1.75f) ? 2.0f : 1.0f;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const float l3 = (__fdiv_rn(a4[2 * i + k / 4], __fmul_rn(sf, l2)) > 1.75f) ? 2.0f : 1.0f;
+        err = __fadd_rn(err, sq_err_ref(stage[(8 * i + k) * st], __fmul_rn(__fmul_rn(sf, l2), l3)));
+      }
+    }
+    if (c == 0 || err < eb) { eb = err; sfb = sf; }
+  }
+  uint32_t bits = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const bool l2 = __fdiv_rn(a8[i], sfb) > 1.75f;
+    bits |= (l2 ? 1u : 0u) << i;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const bool l3 = __fdiv_rn(a4[2 * i + h], __fmul_rn(sfb, l2 ? 2.0f : 1.0f)) > 1.75f;
+      bits |= (l3 ? 1u : 0u) << (8 + 2 * i + h);
+    }
+  }
+  Enc r;
+  r.sf = sfb;
+  r.bits = bits;
+  return r;
+}
+
+// _encode_e6m2 (dev/variants.py:240-246)
+__device__ __forceinline__ float encode_e6m2(float x) {
+  const float xc = fmaxf(x, 1e-30f);
+  const int e = floor_log2_torch(xc);
+  float m = rintf(__fmul_rn(xc, exp2i(2 - e)));
+  m = clampf(m, 4.0f, 8.0f);
+  return clampf(__fmul_rn(m, exp2i(e - 2)), kSfMin, kSfMax);
+}
+
+// ---------------------------------------------------------------- outputs
+__device__ __forceinline__ uint32_t e6m2_code(float sf) {
+  const uint32_t b = __float_as_uint(sf);
+  const int E = (int)(b >> 23) - 127;
+  return ((uint32_t)(E + 48) << 2) | ((b >> 21) & 3u);
+}
+
+__global__ void __launch_bounds__(kConvThreads) convert_kernel(const ConvParams p) {
+  extern __shared__ float smem[];
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= p.ngroups) return;
+  const int st = blockDim.x;
+  float *stage = smem + threadIdx.x;
+  const int64_t bcol = g % p.nb;  // 64-block index within the row
+
+  float x[64];
+  load_group(p, g, x);
+  if (p.smooth_mode != HIF4X_SMOOTH_NONE) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(p.smooth) + bcol * 16;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const float4 s = __ldg(s4 + j);
+      const float sv[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+      for (int n = 0; n < 4; n++)
+        x[4 * j + n] = p.smooth_mode == HIF4X_SMOOTH_MUL ? __fmul_rn(x[4 * j + n], sv[n])
+                                                          : __fdiv_rn(x[4 * j + n], sv[n]);
+    }
+  }
+  if (p.rot_signs != nullptr) rot64_exact(x, __ldg(p.rot_signs + bcol), stage, st);
+  if (p.out_x != nullptr) {
+    float4 *o4 = reinterpret_cast<float4 *>(p.out_x) + g * 16;
+#pragma unroll
+    for (int j = 0; j < 16; j++) o4[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+  }
+  if (p.encode_mode == HIF4X_ENC_NONE) return;
+
+  // signs: neg (x < 0) and zero (x == 0) masks; stage |x|
+  uint64_t neg = 0;
+  float amax = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 64; k++) {
+    const float a = fabsf(x[k]);
+    neg |= (x[k] < 0.0f ? 1ull : 0ull) << k;
+    amax = fmaxf(amax, a);
+    stage[k * st] = a;
+  }
+
+  Enc enc;
+  if (p.encode_mode == HIF4X_ENC_SEARCH) {
+    const float t = fmaxf(__fdiv_rn(amax, 7.0f), 1e-38f);
+    const int e0 = floor_log2_torch(t);
+    enc = (e0 >= -48 && e0 <= 14) ? search_fast(stage, st, e0) : search_generic(stage, st, e0);
+  } else if (p.encode_mode == HIF4X_ENC_FAST) {
+    enc = encode_fast(stage, st, amax);
+  } else {
+    // Algorithm 1 (dev/variants.py:258-287): sf from the peak, lv bits by threshold.
+    enc.sf = encode_e6m2(__fdiv_rn(amax, 7.0f));
+    const float rec = __fdiv_rn(1.0f, enc.sf);
+    uint32_t bits = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      float v16[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float m = stage[(8 * i + 4 * h) * st];
+#pragma unroll
+        for (int k = 1; k < 4; k++) m = fmaxf(m, stage[(8 * i + 4 * h + k) * st]);
+        v16[h] = m;
+      }
+      const float v8 = fmaxf(v16[0], v16[1]);
+      const bool e8 = __fmul_rn(v8, rec) >= 4.0f;
+      bits |= (e8 ? 1u : 0u) << i;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const bool e16 = __fmul_rn(__fmul_rn(v16[h], rec), e8 ? 0.5f : 1.0f) >= 2.0f;
+        bits |= (e16 ? 1u : 0u) << (8 + 2 * i + h);
+      }
+    }
+    enc.bits = bits;
+  }
+
+  // ---- element pass: mant, sign and every requested output
+  const float sf = enc.sf;
+  const bool alg1 = p.encode_mode == HIF4X_ENC_ALG1;
+  const float rec = alg1 ? __fdiv_rn(1.0f, sf) : 0.0f;
+  // Markstein reciprocal of the significand part: unit = sf * 2^(l2+l3)
+  const float ysf = __fdiv_rn(1.0f, sf);
+  uint32_t meta_word = e6m2_code(sf) | ((enc.bits & 0xffu) << 8) | ((enc.bits >> 8) << 16);
+  if (p.sf != nullptr) p.sf[g] = sf;
+  if (p.meta != nullptr) p.meta[g] = meta_word;
+#pragma unroll 1
+  for (int i = 0; i < 8; i++) {
+    const uint32_t l2 = (enc.bits >> i) & 1u;
+    if (p.lv2 != nullptr) p.lv2[g * 8 + i] = l2 ? 2.0f : 1.0f;
+    float mant8[8], sign8[8], unit8[8], deq8[8];
+    uint32_t nib = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int el = 8 * i + k;
+      const uint32_t l3 = (enc.bits >> (8 + 2 * i + k / 4)) & 1u;
+      const float a = stage[el * st];
+      const bool isneg = (neg >> el) & 1ull;
+      const float sg = a == 0.0f ? 0.0f : (isneg ? -1.0f : 1.0f);
+      const float unit = __fmul_rn(__fmul_rn(sf, l2 ? 2.0f : 1.0f), l3 ? 2.0f : 1.0f);
+      float m4;
+      if (!alg1) {
+        // round(|x| / unit * 4) clamped to 7; quotient by Markstein on sf
+        // (the lv factors are powers of two: exact rescaling)
+        const float q0 = __fmul_rn(a, ysf);
+        const float r = __fmaf_rn(-q0, sf, a);
+        float q = __fmaf_rn(r, ysf, q0);
+        q = __fmul_rn(q, (l2 + l3) == 0 ? 4.0f : ((l2 + l3) == 1 ? 2.0f : 1.0f));
+        m4 = q < 4194304.0f ? __fsub_rn(fminf(__fadd_rn(q, kMagic), kMagic + 7.0f), kMagic)
+                                       : fminf(rintf(q), 7.0f);
+      } else {
+        const float xs = __fmul_rn(__fmul_rn(__fmul_rn(a, rec), l2 ? 0.5f : 1.0f), l3 ? 0.5f : 1.0f);
+        m4 = clampf(floorf(__fadd_rn(__fmul_rn(xs, 4.0f), 0.5f)), 0.0f, 7.0f);
+      }
+      const float mant = __fmul_rn(m4, 0.25f);
+      const float sgo = (alg1 && m4 == 0.0f) ? 0.0f : sg;
+      mant8[k] = mant;
+      sign8[k] = sgo;
+      unit8[k] = unit;
+      // value = sign * mant * lv3 * lv2 * sf (exact); keeps -0 for negative zeros
+      deq8[k] = __fmul_rn(__fmul_rn(sgo, mant), __fmul_rn(__fmul_rn(l3 ? 2.0f : 1.0f, l2 ? 2.0f : 1.0f), sf));
+      nib |= ((isneg && !(alg1 && m4 == 0.0f) ? 8u : 0u) | (uint32_t)m4) << (4 * k);
+    }
+    if (p.lv3 != nullptr) {
+      p.lv3[g * 16 + 2 * i] = ((enc.bits >> (8 + 2 * i)) & 1u) ? 2.0f : 1.0f;
+      p.lv3[g * 16 + 2 * i + 1] = ((enc.bits >> (9 + 2 * i)) & 1u) ? 2.0f : 1.0f;
+    }
+    const int64_t e0i = g * 64 + 8 * i;
+    if (p.mant != nullptr) {
+      reinterpret_cast<float4 *>(p.mant + e0i)[0] = make_float4(mant8[0], mant8[1], mant8[2], mant8[3]);
+      reinterpret_cast<float4 *>(p.mant + e0i)[1] = make_float4(mant8[4], mant8[5], mant8[6], mant8[7]);
+    }
+    if (p.sign != nullptr) {
+      reinterpret_cast<float4 *>(p.sign + e0i)[0] = make_float4(sign8[0], sign8[1], sign8[2], sign8[3]);
+      reinterpret_cast<float4 *>(p.sign + e0i)[1] = make_float4(sign8[4], sign8[5], sign8[6], sign8[7]);
+    }
+    if (p.unit != nullptr) {
+      reinterpret_cast<float4 *>(p.unit + e0i)[0] = make_float4(unit8[0], unit8[1], unit8[2], unit8[3]);
+      reinterpret_cast<float4 *>(p.unit + e0i)[1] = make_float4(unit8[4], unit8[5], unit8[6], unit8[7]);
+    }
+    if (p.codes != nullptr) reinterpret_cast<uint32_t *>(p.codes)[g * 8 + i] = nib;
+    if (p.deq != nullptr) {
+      if (p.deq_dtype == HIF4X_DT_F32) {
+        float4 *d4 = reinterpret_cast<float4 *>(static_cast<float *>(p.deq) + e0i);
+        d4[0] = make_float4(deq8[0], deq8[1], deq8[2], deq8[3]);
+        d4[1] = make_float4(deq8[4], deq8[5], deq8[6], deq8[7]);
+      } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int n = 0; n < 4; n++)
+          w[n] = (__float_as_uint(deq8[2 * n]) >> 16) | (__float_as_uint(deq8[2 * n + 1]) & 0xffff0000u);
+        reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.deq) + e0i)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- decoders
+// HiF4 packed -> values; one thread per 8-element sub-block.
+__global__ void decode_packed_kernel(const uint32_t *__restrict__ meta, const uint32_t *__restrict__ codes,
+                                     int64_t nsub, void *out, int out_dtype) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= nsub) return;
+  const int64_t g = t >> 3;
+  const int i = (int)(t & 7);
+  const uint32_t m = __ldg(meta + g);
+  const uint32_t w = __ldcs(codes + t);
+  const int E = (int)((m & 0xffu) >> 2) - 48;
+  const float sf = __fmul_rn(exp2i(E), 1.0f + 0.25f * (float)(m & 3u));
+  const uint32_t l2 = (m >> (8 + i)) & 1u;
+  float v[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const uint32_t l3 = (m >> (16 + 2 * i + k / 4)) & 1u;
+    const uint32_t nib = (w >> (4 * k)) & 15u;
+    const float scale = __fmul_rn(sf, exp2i((int)(l2 + l3) - 2));  // sf * lv2 * lv3 / 4, exact
+    const float mag = __fmul_rn((float)(nib & 7u), scale);
+    v[k] = (nib & 8u) ? -mag : mag;
+  }
+  if (out_dtype == HIF4X_DT_F32) {
+    float4 *o = reinterpret_cast<float4 *>(out) + t * 2;
+    __stcs(o, make_float4(v[0], v[1], v[2], v[3]));
+    __stcs(o + 1, make_float4(v[4], v[5], v[6], v[7]));
+  } else {
+    uint32_t q[4];
+#pragma unroll
+    for (int n = 0; n < 4; n++) q[n] = (__float_as_uint(v[2 * n]) >> 16) | (__float_as_uint(v[2 * n + 1]) & 0xffff0000u);
+    __stcs(reinterpret_cast<uint4 *>(out) + t, make_uint4(q[0], q[1], q[2], q[3]));
+  }
+}
+
+// dict5 -> values, one thread per element: ((((sign*mant)*lv3)*lv2)*sf)
+__global__ void decode_dict5_kernel(const float *sf, const float *lv2, const float *lv3, const float *sign,
+                                    const float *mant, int64_t n, void *out, int out_dtype) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n) return;
+  const int64_t g = e >> 6;
+  const int k = (int)(e & 63);
+  float v = __fmul_rn(sign[e], mant[e]);
+  v = __fmul_rn(v, lv3[g * 16 + k / 4]);
+  v = __fmul_rn(v, lv2[g * 8 + k / 8]);
+  v = __fmul_rn(v, sf[g]);
+  if (out_dtype == HIF4X_DT_F32) static_cast<float *>(out)[e] = v;
+  else static_cast<__nv_bfloat16 *>(out)[e] = __float2bfloat16_rn(v);
+}
+
+__global__ void values_to_params_kernel(const float *q, const float *sf, const float *lv2, const float *lv3,
+                                        int64_t n, float *sign, float *mant) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n) return;
+  const int64_t g = e >> 6;
+  const int k = (int)(e & 63);
+  const float unit = __fmul_rn(__fmul_rn(sf[g], lv2[g * 8 + k / 8]), lv3[g * 16 + k / 4]);
+  const float v = q[e];
+  float m = rintf(__fmul_rn(__fdiv_rn(fabsf(v), unit), 4.0f));
+  mant[e] = __fmul_rn(clampf(m, 0.0f, 7.0f), 0.25f);
+  sign[e] = torch_sign(v);
+}
+
+__global__ void unit_flat_kernel(const float *sf, const float *lv2, const float *lv3, int64_t n, float *unit) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n) return;
+  const int64_t g = e >> 6;
+  const int k = (int)(e & 63);
+  unit[e] = __fmul_rn(__fmul_rn(sf[g], lv2[g * 8 + k / 8]), lv3[g * 16 + k / 4]);
+}
+
+__global__ void pack_dict5_kernel(const float *sf, const float *lv2, const float *lv3, const float *sign,
+                                  const float *mant, int64_t ngroups, uint32_t *meta, uint8_t *codes) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= ngroups) return;
+  uint32_t w = e6m2_code(sf[g]);
+  for (int i = 0; i < 8; i++) w |= (lv2[g * 8 + i] == 2.0f ? 1u : 0u) << (8 + i);
+  for (int j = 0; j < 16; j++) w |= (lv3[g * 16 + j] == 2.0f ? 1u : 0u) << (16 + j);
+  meta[g] = w;
+  for (int i = 0; i < 8; i++) {
+    uint32_t nib = 0;
+    for (int k = 0; k < 8; k++) {
+      const int64_t e = g * 64 + 8 * i + k;
+      nib |= ((sign[e] < 0.0f ? 8u : 0u) | (uint32_t)(mant[e] * 4.0f)) << (4 * k);
+    }
+    reinterpret_cast<uint32_t *>(codes)[g * 8 + i] = nib;
+  }
+}
+
+__global__ void unpack_dict5_kernel(const uint32_t *meta, const uint8_t *codes, int64_t ngroups, float *sf,
+                                    float *lv2, float *lv3, float *sign, float *mant) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= ngroups) return;
+  const uint32_t m = meta[g];
+  const int E = (int)((m & 0xffu) >> 2) - 48;
+  sf[g] = __fmul_rn(exp2i(E), 1.0f + 0.25f * (float)(m & 3u));
+  for (int i = 0; i < 8; i++) lv2[g * 8 + i] = ((m >> (8 + i)) & 1u) ? 2.0f : 1.0f;
+  for (int j = 0; j < 16; j++) lv3[g * 16 + j] = ((m >> (16 + j)) & 1u) ? 2.0f : 1.0f;
+  for (int i = 0; i < 8; i++) {
+    const uint32_t w = reinterpret_cast<const uint32_t *>(codes)[g * 8 + i];
+    for (int k = 0; k < 8; k++) {
+      const uint32_t nib = (w >> (4 * k)) & 15u;
+      const int64_t e = g * 64 + 8 * i + k;
+      mant[e] = 0.25f * (float)(nib & 7u);
+      sign[e] = (nib & 8u) ? -1.0f : ((nib & 7u) ? 1.0f : 0.0f);
+    }
+  }
+}
+
+// NVFP4 -> values, one thread per 16-element scale block.
+__global__ void nvfp4_decode_kernel(int src_kind, const void *src, int src_dtype, const void *scale,
+                                    int scale_dtype, float s_dec, int64_t nblk, void *out, int out_dtype) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nblk) return;
+  float v[16];
+  if (src_kind == HIF4X_SRC_NVFP4_PACKED) {
+    const float s = __fmul_rn(e4m3_to_f32(static_cast<const uint8_t *>(scale)[b]), s_dec);
+    const uint2 w = __ldcs(reinterpret_cast<const uint2 *>(src) + b);
+    const uint32_t ww[2] = {w.x, w.y};
+#pragma unroll
+    for (int n = 0; n < 16; n++) v[n] = bf16_round(__fmul_rn(e2m1_to_f32((ww[n >> 3] >> (4 * (n & 7))) & 15u), s));
+  } else {
+    const float s = scale_dtype == HIF4X_DT_F32 ? static_cast<const float *>(scale)[b]
+                                                : bf16_bits_to_f32(static_cast<const uint16_t *>(scale)[b]);
+#pragma unroll
+    for (int n = 0; n < 16; n++) {
+      const float c = src_dtype == HIF4X_DT_F32 ? static_cast<const float *>(src)[b * 16 + n]
+                                                : bf16_bits_to_f32(static_cast<const uint16_t *>(src)[b * 16 + n]);
+      v[n] = bf16_round(__fmul_rn(c, s));
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < 16; n++) {
+    if (out_dtype == HIF4X_DT_F32) static_cast<float *>(out)[b * 16 + n] = v[n];
+    else static_cast<__nv_bfloat16 *>(out)[b * 16 + n] = __float2bfloat16_rn(v[n]);
+  }
+}
+
+// standalone rotation: one thread per group
+__global__ void __launch_bounds__(kConvThreads) rotate64_kernel(const float *x, const uint64_t *signs, int64_t ngroups,
+                                                                 int64_t nb, float *out) {
+  extern __shared__ float smem[];
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= ngroups) return;
+  float v[64];
+  const float4 *x4 = reinterpret_cast<const float4 *>(x) + g * 16;
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    const float4 a = __ldg(x4 + j);
+    v[4 * j] = a.x; v[4 * j + 1] = a.y; v[4 * j + 2] = a.z; v[4 * j + 3] = a.w;
+  }
+  rot64_exact(v, __ldg(signs + g % nb), smem + threadIdx.x, blockDim.x);
+  float4 *o4 = reinterpret_cast<float4 *>(out) + g * 16;
+#pragma unroll
+  for (int j = 0; j < 16; j++) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+}  // namespace hif4x
+
+// ====================================================================== ABI
+using namespace hif4x;
+
+static inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static inline unsigned nblocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+extern "C" int hif4x_version(void) { return 100; }
+
+extern "C" int hif4x_convert(const hif4x_convert_desc *d, void *stream) {
+  if (d == nullptr || d->rows < 0 || d->cols <= 0 || d->cols % 64 != 0 || d->src == nullptr) return HIF4X_ERR_ARG;
+  if (d->src_kind != HIF4X_SRC_VALUES && d->src_scale == nullptr) return HIF4X_ERR_ARG;
+  if (d->smooth_mode != HIF4X_SMOOTH_NONE && d->smooth == nullptr) return HIF4X_ERR_ARG;
+  if (d->encode_mode < HIF4X_ENC_NONE || d->encode_mode > HIF4X_ENC_ALG1) return HIF4X_ERR_ARG;
+  const void *ptrs[] = {d->src, d->src_scale, d->smooth, d->out_x, d->sign, d->mant, d->deq, d->unit, d->codes};
+  for (const void *q : ptrs)
+    if (q != nullptr && !al16(q)) return HIF4X_ERR_ARG;
+  if (d->src_kind == HIF4X_SRC_NVFP4_PACKED && (reinterpret_cast<uintptr_t>(d->src_scale) & 3u)) return HIF4X_ERR_ARG;
+  if (d->src_kind == HIF4X_SRC_NVFP4_PAIR && d->scale_dtype == HIF4X_DT_BF16 &&
+      (reinterpret_cast<uintptr_t>(d->src_scale) & 7u))
+    return HIF4X_ERR_ARG;
+  if (d->rows == 0) return HIF4X_OK;
+  ConvParams p;
+  p.nb = d->cols / 64;
+  p.ngroups = d->rows * p.nb;
+  p.src_kind = d->src_kind; p.src_dtype = d->src_dtype; p.scale_dtype = d->scale_dtype;
+  p.s_dec = d->s_dec; p.src = d->src; p.src_scale = d->src_scale;
+  p.smooth = d->smooth; p.smooth_mode = d->smooth_mode; p.rot_signs = d->rot_signs;
+  p.encode_mode = d->encode_mode; p.out_x = d->out_x;
+  p.sf = d->sf; p.lv2 = d->lv2; p.lv3 = d->lv3; p.sign = d->sign; p.mant = d->mant;
+  p.meta = d->meta; p.codes = d->codes; p.deq = d->deq; p.deq_dtype = d->deq_dtype; p.unit = d->unit;
+  const size_t smem = 64 * kConvThreads * sizeof(float);
+  convert_kernel<<<nblocks(p.ngroups, kConvThreads), kConvThreads, smem, (cudaStream_t)stream>>>(p);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_nvfp4_decode(const void *carrier, int carrier_dtype, const void *scale, int scale_dtype,
+                                  int64_t rows, int64_t cols, void *out, int out_dtype, void *stream) {
+  if (!carrier || !scale || !out || rows < 0 || cols % 16 != 0) return HIF4X_ERR_ARG;
+  const int64_t nblk = rows * (cols / 16);
+  if (nblk == 0) return HIF4X_OK;
+  nvfp4_decode_kernel<<<nblocks(nblk, 256), 256, 0, (cudaStream_t)stream>>>(
+      HIF4X_SRC_NVFP4_PAIR, carrier, carrier_dtype, scale, scale_dtype, 0.0f, nblk, out, out_dtype);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_nvfp4_decode_packed(const uint8_t *codes, const uint8_t *e4m3, float s_dec, int64_t rows,
+                                         int64_t cols, void *out, int out_dtype, void *stream) {
+  if (!codes || !e4m3 || !out || rows < 0 || cols % 16 != 0 || (reinterpret_cast<uintptr_t>(codes) & 7u))
+    return HIF4X_ERR_ARG;
+  const int64_t nblk = rows * (cols / 16);
+  if (nblk == 0) return HIF4X_OK;
+  nvfp4_decode_kernel<<<nblocks(nblk, 256), 256, 0, (cudaStream_t)stream>>>(
+      HIF4X_SRC_NVFP4_PACKED, codes, 0, e4m3, 0, s_dec, nblk, out, out_dtype);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_rotate64(const float *x, const uint64_t *signs, int64_t rows, int64_t cols, float *out,
+                              void *stream) {
+  if (!x || !signs || !out || rows < 0 || cols % 64 != 0 || !al16(x) || !al16(out)) return HIF4X_ERR_ARG;
+  const int64_t ng = rows * (cols / 64);
+  if (ng == 0) return HIF4X_OK;
+  rotate64_kernel<<<nblocks(ng, kConvThreads), kConvThreads, 64 * kConvThreads * sizeof(float),
+                    (cudaStream_t)stream>>>(x, signs, ng, cols / 64, out);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+static int encode_values(const float *x, int mode, int64_t rows, int64_t cols, float *sf, float *lv2, float *lv3,
+                         float *sign, float *mant, void *stream) {
+  hif4x_convert_desc d = {};
+  d.rows = rows; d.cols = cols; d.src_kind = HIF4X_SRC_VALUES; d.src_dtype = HIF4X_DT_F32; d.src = x;
+  d.encode_mode = mode; d.sf = sf; d.lv2 = lv2; d.lv3 = lv3; d.sign = sign; d.mant = mant;
+  return hif4x_convert(&d, stream);
+}
+
+extern "C" int hif4x_encode_search(const float *x, int64_t rows, int64_t cols, float *sf, float *lv2, float *lv3,
+                                   float *sign, float *mant, void *stream) {
+  return encode_values(x, HIF4X_ENC_SEARCH, rows, cols, sf, lv2, lv3, sign, mant, stream);
+}
+
+extern "C" int hif4x_encode_alg1(const float *x, int64_t rows, int64_t cols, float *sf, float *lv2, float *lv3,
+                                 float *sign, float *mant, void *stream) {
+  return encode_values(x, HIF4X_ENC_ALG1, rows, cols, sf, lv2, lv3, sign, mant, stream);
+}
+
+extern "C" int hif4x_decode_dict5(const float *sf, const float *lv2, const float *lv3, const float *sign,
+                                  const float *mant, int64_t rows, int64_t cols, void *out, int out_dtype,
+                                  void *stream) {
+  if (!sf || !lv2 || !lv3 || !sign || !mant || !out || rows < 0 || cols % 64 != 0) return HIF4X_ERR_ARG;
+  const int64_t n = rows * cols;
+  if (n == 0) return HIF4X_OK;
+  decode_dict5_kernel<<<nblocks(n, 256), 256, 0, (cudaStream_t)stream>>>(sf, lv2, lv3, sign, mant, n, out, out_dtype);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_decode_packed(const uint32_t *meta, const uint8_t *codes, int64_t rows, int64_t cols, void *out,
+                                   int out_dtype, void *stream) {
+  if (!meta || !codes || !out || rows < 0 || cols % 64 != 0 || !al16(codes) || !al16(out)) return HIF4X_ERR_ARG;
+  const int64_t nsub = rows * (cols / 8);
+  if (nsub == 0) return HIF4X_OK;
+  decode_packed_kernel<<<nblocks(nsub, 256), 256, 0, (cudaStream_t)stream>>>(
+      meta, reinterpret_cast<const uint32_t *>(codes), nsub, out, out_dtype);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_values_to_params(const float *q, const float *sf, const float *lv2, const float *lv3,
+                                      int64_t rows, int64_t cols, float *sign, float *mant, void *stream) {
+  if (!q || !sf || !lv2 || !lv3 || !sign || !mant || rows < 0 || cols % 64 != 0) return HIF4X_ERR_ARG;
+  const int64_t n = rows * cols;
+  if (n == 0) return HIF4X_OK;
+  values_to_params_kernel<<<nblocks(n, 256), 256, 0, (cudaStream_t)stream>>>(q, sf, lv2, lv3, n, sign, mant);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_unit_flat(const float *sf, const float *lv2, const float *lv3, int64_t rows, int64_t cols,
+                               float *unit, void *stream) {
+  if (!sf || !lv2 || !lv3 || !unit || rows < 0 || cols % 64 != 0) return HIF4X_ERR_ARG;
+  const int64_t n = rows * cols;
+  if (n == 0) return HIF4X_OK;
+  unit_flat_kernel<<<nblocks(n, 256), 256, 0, (cudaStream_t)stream>>>(sf, lv2, lv3, n, unit);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_pack_dict5(const float *sf, const float *lv2, const float *lv3, const float *sign,
+                                const float *mant, int64_t rows, int64_t cols, uint32_t *meta, uint8_t *codes,
+                                void *stream) {
+  if (!sf || !lv2 || !lv3 || !sign || !mant || !meta || !codes || rows < 0 || cols % 64 != 0) return HIF4X_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(codes) & 3u) return HIF4X_ERR_ARG;
+  const int64_t ng = rows * (cols / 64);
+  if (ng == 0) return HIF4X_OK;
+  pack_dict5_kernel<<<nblocks(ng, 128), 128, 0, (cudaStream_t)stream>>>(sf, lv2, lv3, sign, mant, ng, meta, codes);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_unpack_dict5(const uint32_t *meta, const uint8_t *codes, int64_t rows, int64_t cols, float *sf,
+                                  float *lv2, float *lv3, float *sign, float *mant, void *stream) {
+  if (!sf || !lv2 || !lv3 || !sign || !mant || !meta || !codes || rows < 0 || cols % 64 != 0) return HIF4X_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(codes) & 3u) return HIF4X_ERR_ARG;
+  const int64_t ng = rows * (cols / 64);
+  if (ng == 0) return HIF4X_OK;
+  unpack_dict5_kernel<<<nblocks(ng, 128), 128, 0, (cudaStream_t)stream>>>(meta, codes, ng, sf, lv2, lv3, sign, mant);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}

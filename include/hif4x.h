@@ -1,0 +1,162 @@
+/*
+ * hif4x.h -- C ABI of the B200 NVFP4 -> HiF4 conversion engine.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream and returns an
+ * int status (HIF4X_OK = 0; > 0 recoverable, the caller takes the
+ * reference's fallback branch; < 0 a caller or launch error).  Pointers are
+ * borrowed: the library never frees caller memory.  Tensors are dense
+ * row-major; a matrix (R, C) has C % 64 == 0 unless noted.
+ *
+ * Each declaration names the reference function it replaces (paths relative
+ * to the reference project, openaddr/hif4-contest).
+ *
+ * Formats
+ *   NVFP4 packed : codes uint8 (R, C/2), nibble = sign<<3 | E2M1 index,
+ *                  element 2i in the low nibble of byte i; e4m3 uint8
+ *                  (R, C/16) one E4M3 scale per 16 elements; fp32 s_dec.
+ *   NVFP4 pair   : the reference's [carrier, scale] pair: carrier (R, C)
+ *                  bf16 or fp32 holding E2M1 values, scale (R, C/16) fp32
+ *                  or bf16 (example/solution/solution.py:49-57).
+ *   dict5        : the reference's HiF4 parameters as five fp32 arrays:
+ *                  sf (R, C/64), lv2 (R, C/64, 8), lv3 (R, C/64, 16),
+ *                  sign (R, C), mant (R, C)  (example/self_check.py:75-95).
+ *   HiF4 packed  : meta uint32 (R, C/64): bits 0-7 E6M2 code
+ *                  ((E+48)<<2 | M), bits 8-15 E1_8, bits 16-31 E1_16;
+ *                  codes uint8 (R, C/2): nibble = sign<<3 | mant*4
+ *                  (hif4_paper.txt section II-A layout, 4.5 bit/elem).
+ */
+#ifndef HIF4X_H_
+#define HIF4X_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define HIF4X_OK 0
+#define HIF4X_NOT_PD 1            /* Cholesky met a non-positive pivot        */
+#define HIF4X_TIMEOUT 2           /* a bounded device wait gave up            */
+#define HIF4X_ERR_ARG (-1)        /* bad pointer / size / alignment           */
+#define HIF4X_ERR_LAUNCH (-2)     /* CUDA launch or runtime error             */
+#define HIF4X_ERR_UNSUPPORTED (-3)
+
+/* ---- enums ------------------------------------------------------------- */
+#define HIF4X_DT_F32 0
+#define HIF4X_DT_BF16 1
+
+#define HIF4X_SRC_NVFP4_PACKED 0  /* src = codes, src_scale = e4m3, s_dec     */
+#define HIF4X_SRC_NVFP4_PAIR 1    /* src = carrier, src_scale = scale         */
+#define HIF4X_SRC_VALUES 2        /* src = values (src_dtype), no decode      */
+
+#define HIF4X_SMOOTH_NONE 0
+#define HIF4X_SMOOTH_MUL 1        /* x * s[c]  (activations)                  */
+#define HIF4X_SMOOTH_DIV 2        /* x / s[c]  (weights)                      */
+
+#define HIF4X_ENC_NONE 0          /* decode / transform only                  */
+#define HIF4X_ENC_SEARCH 1        /* 6-candidate searched encode              */
+#define HIF4X_ENC_FAST 2          /* 4-candidate greedy-lv encode             */
+#define HIF4X_ENC_ALG1 3          /* paper Algorithm 1 (standard quantizer)   */
+
+/* One fused pass: source decode -> optional per-channel smoothing ->
+ * optional 64-point block rotation -> optional HiF4 encode, writing any
+ * subset of the outputs (NULL = not written).  One thread per 64-group; the
+ * input is read once. */
+typedef struct hif4x_convert_desc {
+  int64_t rows, cols;
+  int src_kind;              /* HIF4X_SRC_*                                   */
+  int src_dtype;             /* carrier / values dtype (HIF4X_DT_*)           */
+  int scale_dtype;           /* pair scale dtype (HIF4X_DT_*)                 */
+  float s_dec;               /* packed NVFP4 tensor scale                     */
+  const void *src;           /* codes | carrier | values                      */
+  const void *src_scale;     /* e4m3 | scale | NULL                           */
+  const float *smooth;       /* (cols,) per-channel factor or NULL            */
+  int smooth_mode;           /* HIF4X_SMOOTH_*                                */
+  const uint64_t *rot_signs; /* (cols/64,) sign masks, NULL = no rotation     */
+  int encode_mode;           /* HIF4X_ENC_*                                   */
+  float *out_x;              /* (R, C) transformed fp32 values                */
+  float *sf, *lv2, *lv3, *sign, *mant; /* dict5                               */
+  uint32_t *meta;            /* packed HiF4 metadata                          */
+  uint8_t *codes;            /* packed HiF4 nibbles                           */
+  void *deq;                 /* (R, C) HiF4-decoded values                    */
+  int deq_dtype;             /* HIF4X_DT_*                                    */
+  float *unit;               /* (R, C) sf*lv2*lv3                             */
+} hif4x_convert_desc;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int hif4x_version(void);
+
+/* Fused convert.  Replaces, in one launch, the chain
+ *   dequantize_nvfp4 (example/solution/solution.py:49-57)
+ *   -> a * s / w / s smoothing (solution.py:871-873, 1049)
+ *   -> _rot_blocks (solution.py:222-245)
+ *   -> _quantize_weighted / _quant_chunk (solution.py:744-770, 60-124)
+ *      | _quant_weight_fast (solution.py:787-823)
+ *      | quant_alg1 (dev/variants.py:249-287). */
+int hif4x_convert(const hif4x_convert_desc *desc, void *stream);
+
+/* dequantize_nvfp4, pair form (example/solution/solution.py:49-57,
+ * dev/hif4.py:17-20).  out (R, C) of out_dtype; C % 16 == 0. */
+int hif4x_nvfp4_decode(const void *carrier, int carrier_dtype, const void *scale, int scale_dtype,
+                       int64_t rows, int64_t cols, void *out, int out_dtype, void *stream);
+
+/* dequantize_nvfp4 of the packed form (same result as the pair form whose
+ * scale is fp32(e4m3) * s_dec). */
+int hif4x_nvfp4_decode_packed(const uint8_t *codes, const uint8_t *e4m3, float s_dec, int64_t rows,
+                              int64_t cols, void *out, int out_dtype, void *stream);
+
+/* _rot_blocks (example/solution/solution.py:222-245): bit-exact with the
+ * reference's fp32 einsum.  signs may be NULL (then the reference's seeded
+ * signs for block b = 0..cols/64-1 are used from a library-owned table). */
+int hif4x_rotate64(const float *x, const uint64_t *signs, int64_t rows, int64_t cols, float *out,
+                   void *stream);
+
+/* Host: the reference's rotation sign masks.  Bit e of out[b] is set when
+ * torch.Generator().manual_seed(seed0 + b) draws rand(len)[e] >= 0.5, i.e.
+ * sign -1 (solution.py:240-242 with seed0 777, len 64; solution.py:1114-1115
+ * with seed0 0xA5A5 + dh, len dh <= 64 per word). */
+int hif4x_rot_signs(int64_t n_vec, int64_t len, uint32_t seed0, uint64_t *out_host);
+
+/* _quantize_weighted(x, ones) (example/solution/solution.py:744-770) on fp32
+ * values; writes dict5 (all five non-NULL). */
+int hif4x_encode_search(const float *x, int64_t rows, int64_t cols, float *sf, float *lv2,
+                        float *lv3, float *sign, float *mant, void *stream);
+
+/* quant_alg1 (dev/variants.py:249-287), dict5 out. */
+int hif4x_encode_alg1(const float *x, int64_t rows, int64_t cols, float *sf, float *lv2, float *lv3,
+                      float *sign, float *mant, void *stream);
+
+/* hif4_dequantize / _deq_params (dev/hif4.py:37-38, solution.py:1090-1092):
+ * dict5 -> values (out_dtype). */
+int hif4x_decode_dict5(const float *sf, const float *lv2, const float *lv3, const float *sign,
+                       const float *mant, int64_t rows, int64_t cols, void *out, int out_dtype,
+                       void *stream);
+
+/* HiF4 packed -> values (out_dtype); the packed twin of hif4_dequantize. */
+int hif4x_decode_packed(const uint32_t *meta, const uint8_t *codes, int64_t rows, int64_t cols,
+                        void *out, int out_dtype, void *stream);
+
+/* _values_to_params (example/solution/solution.py:734-741): re-encode values
+ * q onto fixed sf/lv2/lv3; writes sign and mant (dict5 form). */
+int hif4x_values_to_params(const float *q, const float *sf, const float *lv2, const float *lv3,
+                           int64_t rows, int64_t cols, float *sign, float *mant, void *stream);
+
+/* _params_unit_flat (example/solution/solution.py:726-731): unit (R, C). */
+int hif4x_unit_flat(const float *sf, const float *lv2, const float *lv3, int64_t rows, int64_t cols,
+                    float *unit, void *stream);
+
+/* dict5 <-> HiF4 packed.  Unpack writes sign = 0 where mant == 0 and the
+ * packed sign bit is clear, -1 where it is set (the packed form keeps the
+ * value, not the sign of a zero element). */
+int hif4x_pack_dict5(const float *sf, const float *lv2, const float *lv3, const float *sign,
+                     const float *mant, int64_t rows, int64_t cols, uint32_t *meta, uint8_t *codes,
+                     void *stream);
+int hif4x_unpack_dict5(const uint32_t *meta, const uint8_t *codes, int64_t rows, int64_t cols,
+                       float *sf, float *lv2, float *lv3, float *sign, float *mant, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HIF4X_H_ */
