@@ -717,7 +717,9 @@ static inline unsigned nblocks(int64_t n, int t) { return (unsigned)((n + t - 1)
 extern "C" int hif4x_version(void) { return 100; }
 
 extern "C" int hif4x_convert(const hif4x_convert_desc *d, void *stream) {
-  if (d == nullptr || d->rows < 0 || d->cols <= 0 || d->cols % 64 != 0 || d->src == nullptr) return HIF4X_ERR_ARG;
+  if (d == nullptr || d->rows < 0 || d->cols <= 0 || d->cols % 64 != 0) return HIF4X_ERR_ARG;
+  if (d->rows == 0) return HIF4X_OK;  // empty tensors may carry null pointers
+  if (d->src == nullptr) return HIF4X_ERR_ARG;
   if (d->src_kind != HIF4X_SRC_VALUES && d->src_scale == nullptr) return HIF4X_ERR_ARG;
   if (d->smooth_mode != HIF4X_SMOOTH_NONE && d->smooth == nullptr) return HIF4X_ERR_ARG;
   if (d->encode_mode < HIF4X_ENC_NONE || d->encode_mode > HIF4X_ENC_ALG1) return HIF4X_ERR_ARG;
@@ -728,7 +730,6 @@ extern "C" int hif4x_convert(const hif4x_convert_desc *d, void *stream) {
   if (d->src_kind == HIF4X_SRC_NVFP4_PAIR && d->scale_dtype == HIF4X_DT_BF16 &&
       (reinterpret_cast<uintptr_t>(d->src_scale) & 7u))
     return HIF4X_ERR_ARG;
-  if (d->rows == 0) return HIF4X_OK;
   ConvParams p;
   p.nb = d->cols / 64;
   p.ngroups = d->rows * p.nb;
