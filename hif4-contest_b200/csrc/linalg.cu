@@ -1,0 +1,542 @@
+// linalg.cu -- fp32 dense linear algebra for the calibration pipeline:
+//   * strided-batched GEMM  C = alpha * op(A) op(B) + beta * C  (row-major)
+//   * damped Cholesky -> upper factor of the inverse (GPTQ's Hinv)
+//   * GPTQ column-sequential quantize-and-propagate inside a column block
+//
+// The GEMM is a register-tiled SIMT kernel (128x128x8 CTA tile, 8x8 per
+// thread, double-buffered shared memory), fp32 in and out with fp32
+// accumulation, so every product matches the reference's fp32 matmuls to
+// rounding.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace hif4x {
+
+// --------------------------------------------------------------------------
+// GEMM
+constexpr int GBM = 128, GBN = 128, GBK = 8, GTHREADS = 256;
+
+struct GemmArgs {
+  int ta, tb;
+  int64_t M, N, K;
+  float alpha, beta;
+  const float *A;
+  int64_t lda, sA;
+  const float *B;
+  int64_t ldb, sB;
+  float *C;
+  int64_t ldc, sC;
+};
+
+__global__ void __launch_bounds__(GTHREADS) gemm_kernel(const GemmArgs g) {
+  __shared__ __align__(16) float As[2][GBK][GBM];
+  __shared__ __align__(16) float Bs[2][GBK][GBN];
+  const int64_t bz = blockIdx.z;
+  const float *A = g.A + bz * g.sA;
+  const float *B = g.B + bz * g.sB;
+  float *C = g.C + bz * g.sC;
+  const int64_t m0 = (int64_t)blockIdx.y * GBM, n0 = (int64_t)blockIdx.x * GBN;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;  // 16 x 16 threads, each 8x8 outputs
+
+  // each thread loads 4 A elements and 4 B elements per K-tile
+  auto loadA = [&](int64_t k0, float (&ra)[4]) {
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int e = tid + r * GTHREADS;  // 0..1023 over (BK x BM)
+      int mm, kk;
+      if (g.ta) { kk = e / GBM; mm = e % GBM; }   // A stored K x M: contiguous in m
+      else { mm = e / GBK; kk = e % GBK; }        // A stored M x K: contiguous in k
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      float v = 0.0f;
+      if (gm < g.M && gk < g.K) v = g.ta ? A[gk * g.lda + gm] : A[gm * g.lda + gk];
+      ra[r] = v;
+    }
+  };
+  auto storeA = [&](int buf, const float (&ra)[4]) {
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int e = tid + r * GTHREADS;
+      int mm, kk;
+      if (g.ta) { kk = e / GBM; mm = e % GBM; }
+      else { mm = e / GBK; kk = e % GBK; }
+      As[buf][kk][mm] = ra[r];
+    }
+  };
+  auto loadB = [&](int64_t k0, float (&rb)[4]) {
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int e = tid + r * GTHREADS;
+      int nn, kk;
+      if (g.tb) { nn = e / GBK; kk = e % GBK; }   // B stored N x K: contiguous in k
+      else { kk = e / GBN; nn = e % GBN; }        // B stored K x N: contiguous in n
+      const int64_t gn = n0 + nn, gk = k0 + kk;
+      float v = 0.0f;
+      if (gn < g.N && gk < g.K) v = g.tb ? B[gn * g.ldb + gk] : B[gk * g.ldb + gn];
+      rb[r] = v;
+    }
+  };
+  auto storeB = [&](int buf, const float (&rb)[4]) {
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int e = tid + r * GTHREADS;
+      int nn, kk;
+      if (g.tb) { nn = e / GBK; kk = e % GBK; }
+      else { kk = e / GBN; nn = e % GBN; }
+      Bs[buf][kk][nn] = rb[r];
+    }
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+
+  float ra[4], rb[4];
+  loadA(0, ra);
+  loadB(0, rb);
+  storeA(0, ra);
+  storeB(0, rb);
+  __syncthreads();
+  const int64_t nk = (g.K + GBK - 1) / GBK;
+  for (int64_t t = 0; t < nk; t++) {
+    const int buf = (int)(t & 1);
+    if (t + 1 < nk) {
+      loadA((t + 1) * GBK, ra);
+      loadB((t + 1) * GBK, rb);
+    }
+#pragma unroll
+    for (int kk = 0; kk < GBK; kk++) {
+      float a[8], b[8];
+      const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][64 + tx * 4]);
+      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (t + 1 < nk) {
+      storeA(buf ^ 1, ra);
+      storeB(buf ^ 1, rb);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int64_t gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (gm >= g.M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int64_t gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      if (gn >= g.N) continue;
+      float *cp = C + gm * g.ldc + gn;
+      const float v = g.alpha * acc[i][j];
+      *cp = g.beta == 0.0f ? v : fmaf(g.beta, *cp, v);
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Cholesky building blocks (lower, in place, row-major n x n, leading dim ld)
+constexpr int CB = 64;  // panel width
+
+// Factor the CB x CB (or smaller) diagonal block at (k, k) in place; one CTA.
+// info = 1 on a non-positive or non-finite pivot.
+__global__ void __launch_bounds__(256) potrf_diag_kernel(float *A, int64_t ld, int64_t k, int b, int *info) {
+  __shared__ float S[CB][CB + 1];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < b * b; e += blockDim.x) S[e / b][e % b] = A[(k + e / b) * ld + k + e % b];
+  __syncthreads();
+  for (int j = 0; j < b; j++) {
+    if (tid == 0) {
+      const float p = S[j][j];
+      if (!(p > 0.0f) || !isfinite(p)) {
+        atomicExch(info, 1);
+        S[j][j] = 1.0f;
+      } else {
+        S[j][j] = sqrtf(p);
+      }
+    }
+    __syncthreads();
+    const float djj = S[j][j];
+    for (int i = j + 1 + tid; i < b; i += blockDim.x) S[i][j] = S[i][j] / djj;
+    __syncthreads();
+    // rank-1 update of the trailing lower part
+    for (int e = tid; e < b * b; e += blockDim.x) {
+      const int r = e / b, c = e % b;
+      if (c > j && r >= c) S[r][c] = fmaf(-S[r][j], S[c][j], S[r][c]);
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < b * b; e += blockDim.x) {
+    const int r = e / b, c = e % b;
+    A[(k + r) * ld + k + c] = (c <= r) ? S[r][c] : 0.0f;
+  }
+}
+
+// Rows below the diagonal block: X <- X * L_kk^-T (forward substitution per row).
+__global__ void __launch_bounds__(128) trsm_panel_kernel(float *A, int64_t ld, int64_t n, int64_t k, int b) {
+  __shared__ float Lk[CB][CB + 1];
+  for (int e = threadIdx.x; e < b * b; e += blockDim.x) Lk[e / b][e % b] = A[(k + e / b) * ld + k + e % b];
+  __syncthreads();
+  const int64_t r = k + b + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  float x[CB];
+  float *row = A + r * ld + k;
+#pragma unroll
+  for (int j = 0; j < CB; j++) x[j] = j < b ? row[j] : 0.0f;
+#pragma unroll
+  for (int j = 0; j < CB; j++) {
+    if (j < b) {
+      float s = x[j];
+#pragma unroll
+      for (int i = 0; i < j; i++) s = fmaf(-x[i], Lk[j][i], s);
+      x[j] = s / Lk[j][j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < CB; j++)
+    if (j < b) row[j] = x[j];
+}
+
+// In-place inverse of a small lower-triangular block (b <= CB); one CTA.
+__global__ void __launch_bounds__(CB) trtri_diag_kernel(float *A, int64_t ld, int64_t k, int b) {
+  __shared__ float L[CB][CB + 1];
+  __shared__ float X[CB][CB + 1];
+  for (int e = threadIdx.x; e < b * b; e += blockDim.x) L[e / b][e % b] = A[(k + e / b) * ld + k + e % b];
+  __syncthreads();
+  // column c of X solves L x = e_c (forward substitution), one thread per column
+  const int c = threadIdx.x;
+  if (c < b) {
+    for (int i = 0; i < b; i++) {
+      float s = (i == c) ? 1.0f : 0.0f;
+      for (int j = c; j < i; j++) s = fmaf(-L[i][j], X[j][c], s);
+      X[i][c] = (i < c) ? 0.0f : s / L[i][i];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
+    const int r = e / b, cc = e % b;
+    A[(k + r) * ld + k + cc] = (cc <= r) ? X[r][cc] : 0.0f;
+  }
+}
+
+// out[i][j] = in[n-1-i][n-1-j] (batched, square)
+__global__ void reverse_square_kernel(const float *in, float *out, int64_t n, int64_t nn_total) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nn_total) return;
+  const int64_t b = e / (n * n), r = (e / n) % n, c = e % n;
+  out[e] = in[b * n * n + (n - 1 - r) * n + (n - 1 - c)];
+}
+
+// Add the reference's damping d = max(mean(diag), 1e-30) * damp to the diagonal
+// (example/solution/solution.py:290-295), one CTA per matrix.
+__global__ void __launch_bounds__(1024) damp_diag_kernel(float *A, int64_t n, float damp) {
+  float *M = A + (int64_t)blockIdx.x * n * n;
+  __shared__ float red[32];
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += M[i * n + i];
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float d = fmaxf(red[0] / (float)n, 1e-30f) * damp;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) M[i * n + i] += d;
+}
+
+__global__ void zero_upper_kernel(float *A, int64_t n, int64_t total) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= total) return;
+  const int64_t r = (e / n) % n, c = e % n;
+  if (c > r) A[e] = 0.0f;
+}
+
+// --------------------------------------------------------------------------
+// GPTQ: one CTA of 128 threads per 128 rows; thread t owns row r0 + t.
+// For the column block [i1, i1+nb): quantize column i to the unit grid
+//   m = clamp(round(|w| / u * 4), 0, 7) * 0.25;  q = (w >= 0 ? 1 : -1) * m * u
+// record E[:, i] = (w - q) / U[i][i] and propagate w[:, j] -= E[:, i] * U[i][j]
+// for j > i inside the block (example/solution/solution.py:316-326).
+constexpr int GQ_THREADS = 128;
+constexpr int GQ_BLK = 128;
+
+__global__ void __launch_bounds__(GQ_THREADS) gptq_block_kernel(float *W, const float *unit, const float *U,
+                                                                  float *Q, float *E, int64_t R, int64_t C,
+                                                                  int64_t i1, int nb, int64_t bstride_rows,
+                                                                  int64_t bstride_u) {
+  extern __shared__ float sm[];
+  float *Hs = sm;                        // [nb][nb] block of U
+  float *Ws = sm + GQ_BLK * GQ_BLK;      // [nb][GQ_THREADS] row slices, column-major per thread
+  const int64_t bz = blockIdx.y;
+  W += bz * bstride_rows * C;
+  unit += bz * bstride_rows * C;
+  Q += bz * bstride_rows * C;
+  E += bz * bstride_rows * GQ_BLK;
+  U += bz * bstride_u;
+  const int t = threadIdx.x;
+  for (int e = t; e < nb * nb; e += GQ_THREADS) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
+  const int64_t r = (int64_t)blockIdx.x * GQ_THREADS + t;
+  const bool live = r < R;
+  if (live)
+    for (int j = 0; j < nb; j++) Ws[j * GQ_THREADS + t] = W[r * C + i1 + j];
+  __syncthreads();
+  if (!live) return;
+  for (int i = 0; i < nb; i++) {
+    const float w = Ws[i * GQ_THREADS + t];
+    const float u = unit[r * C + i1 + i];
+    float m = rintf(__fmul_rn(__fdiv_rn(fabsf(w), u), 4.0f));
+    m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
+    const float q = __fmul_rn(__fmul_rn(w >= 0.0f ? 1.0f : -1.0f, m), u);
+    Q[r * C + i1 + i] = q;
+    const float dii = fmaxf(Hs[i * nb + i], 1e-30f);
+    const float err = __fdiv_rn(__fsub_rn(w, q), dii);
+    E[r * GQ_BLK + i] = err;
+    for (int j = i + 1; j < nb; j++) Ws[j * GQ_THREADS + t] = fmaf(-err, Hs[i * nb + j], Ws[j * GQ_THREADS + t]);
+  }
+  for (int j = 0; j < nb; j++) W[r * C + i1 + j] = Ws[j * GQ_THREADS + t];
+}
+
+// --------------------------------------------------------------------------
+// Greedy top-1 lattice refinement, one CTA per row (example/solution/
+// solution.py:428-663): per round, over the row's C columns,
+//   g = d^2 * G[c][c] - 2 d |M|,  legal if v4 stays in [-7, 7] moving against
+//   the sign of M;  pick the smallest g (first index on ties); if g < 0 flip
+//   v4[idx] += dr (dr = +1 if M[idx] < 0 else -1) and M += dr * d[idx] * G[idx].
+// A row without an improving legal flip never flips again (its state does not
+// change), so it stops.  Each thread owns RC columns in registers.
+constexpr int RC = 8;
+
+__global__ void __launch_bounds__(1024) refine_rows_kernel(float *M, float *v4, const float *d, const float *G,
+                                                           int64_t T, int64_t C, int rounds, int *flips) {
+  __shared__ float rg[32];
+  __shared__ int ri[32];
+  __shared__ float s_coef;
+  __shared__ int s_idx;
+  const int64_t row = blockIdx.x;
+  if (row >= T) return;
+  const int t = threadIdx.x;
+  const int nthr = blockDim.x;
+  float m[RC], v[RC], dd[RC], d2c[RC];
+#pragma unroll
+  for (int k = 0; k < RC; k++) {
+    const int64_t c = (int64_t)k * nthr + t;
+    if (c < C) {
+      m[k] = M[row * C + c];
+      v[k] = v4[row * C + c];
+      dd[k] = d[row * C + c];
+      d2c[k] = __fmul_rn(__fmul_rn(dd[k], dd[k]), G[c * C + c]);
+    } else {
+      m[k] = 0.0f; v[k] = 0.0f; dd[k] = 0.0f; d2c[k] = 0.0f;
+    }
+  }
+  int nflip = 0;
+  for (int rd = 0; rd < rounds; rd++) {
+    float best = INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int k = 0; k < RC; k++) {
+      const int64_t c = (int64_t)k * nthr + t;
+      if (c < C) {
+        const bool up = m[k] < 0.0f;
+        const bool ill = up ? (v[k] >= 7.0f) : (v[k] <= -7.0f);
+        const float g = ill ? INFINITY : fmaf(fabsf(m[k]), -2.0f * dd[k], d2c[k]);
+        if (g < best) { best = g; bi = (int)c; }
+      }
+    }
+    // block argmin, smallest index on ties
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float og = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (og < best || (og == best && oi < bi)) { best = og; bi = oi; }
+    }
+    if ((t & 31) == 0) { rg[t >> 5] = best; ri[t >> 5] = bi; }
+    __syncthreads();
+    if (t < 32) {
+      float b2 = t < (nthr >> 5) ? rg[t] : INFINITY;
+      int i2 = t < (nthr >> 5) ? ri[t] : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float og = __shfl_xor_sync(0xffffffffu, b2, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i2, o);
+        if (og < b2 || (og == b2 && oi < i2)) { b2 = og; i2 = oi; }
+      }
+      if (t == 0) { s_idx = (b2 < 0.0f) ? i2 : -1; }
+    }
+    __syncthreads();
+    const int idx = s_idx;
+    if (idx < 0) break;  // frozen row
+    // owner applies the flip and publishes the coefficient
+    if (idx % nthr == t) {
+      const int k = idx / nthr;
+#pragma unroll
+      for (int kk = 0; kk < RC; kk++)
+        if (kk == k) {
+          const float dr = m[kk] < 0.0f ? 1.0f : -1.0f;
+          v[kk] += dr;
+          s_coef = dr * dd[kk];
+        }
+    }
+    __syncthreads();
+    const float coef = s_coef;
+    const float *gr = G + (int64_t)idx * C;
+#pragma unroll
+    for (int k = 0; k < RC; k++) {
+      const int64_t c = (int64_t)k * nthr + t;
+      if (c < C) m[k] = fmaf(coef, __ldg(gr + c), m[k]);
+    }
+    nflip++;
+    __syncthreads();
+  }
+#pragma unroll
+  for (int k = 0; k < RC; k++) {
+    const int64_t c = (int64_t)k * nthr + t;
+    if (c < C) {
+      M[row * C + c] = m[k];
+      v4[row * C + c] = v[k];
+    }
+  }
+  if (t == 0 && flips != nullptr) flips[row] = nflip;
+}
+
+}  // namespace hif4x
+
+// ====================================================================== ABI
+using namespace hif4x;
+
+static inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+extern "C" int hif4x_gemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                          int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
+                          int64_t ldc, int64_t strideC, int64_t batch, void *stream) {
+  if (M < 0 || N < 0 || K < 0 || batch < 0) return HIF4X_ERR_ARG;
+  if (M == 0 || N == 0 || batch == 0) return HIF4X_OK;
+  if (!A || !B || !C || batch > 65535) return HIF4X_ERR_ARG;
+  GemmArgs g{ta, tb, M, N, K, alpha, beta, A, lda, strideA, B, ldb, strideB, C, ldc, strideC};
+  dim3 grid(nblk(N, GBN), nblk(M, GBM), (unsigned)batch);
+  if (grid.y > 65535) return HIF4X_ERR_ARG;
+  gemm_kernel<<<grid, GTHREADS, 0, (cudaStream_t)stream>>>(g);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+// Lower Cholesky in place (row-major, ld = n), blocked right-looking.
+static int potrf_lower(float *A, int64_t n, int *info_dev, cudaStream_t s) {
+  for (int64_t k = 0; k < n; k += CB) {
+    const int b = (int)std::min<int64_t>(CB, n - k);
+    potrf_diag_kernel<<<1, 256, 0, s>>>(A, n, k, b, info_dev);
+    const int64_t rest = n - k - b;
+    if (rest > 0) {
+      trsm_panel_kernel<<<nblk(rest, 128), 128, 0, s>>>(A, n, n, k, b);
+      // trailing update A22 -= P P^T  (P = A[k+b:, k:k+b])
+      const float *P = A + (k + b) * n + k;
+      int st = hif4x_gemm(0, 1, rest, rest, b, -1.0f, P, n, 0, P, n, 0, 1.0f, A + (k + b) * n + (k + b), n, 0, 1, s);
+      if (st) return st;
+    }
+  }
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+// In-place inverse of a lower-triangular n x n block at A (leading dim ld):
+// inv([[A11, 0], [A21, A22]]) = [[A11^-1, 0], [-A22^-1 A21 A11^-1, A22^-1]].
+static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_t s) {
+  if (n <= CB) {
+    trtri_diag_kernel<<<1, CB, 0, s>>>(A, ld, 0, (int)n);
+    HIF4X_CHECK_LAUNCH();
+    return HIF4X_OK;
+  }
+  int64_t n1 = ((n / 2 + CB - 1) / CB) * CB;
+  const int64_t n2 = n - n1;
+  float *A11 = A, *A21 = A + n1 * ld, *A22 = A + n1 * ld + n1;
+  int st = trtri_lower(A11, n1, ld, work, s);
+  if (st) return st;
+  st = trtri_lower(A22, n2, ld, work, s);
+  if (st) return st;
+  // T = A21 * A11^-1  (n2 x n1) into work; A21 = -A22^-1 * T
+  st = hif4x_gemm(0, 0, n2, n1, n1, 1.0f, A21, ld, 0, A11, ld, 0, 0.0f, work, n1, 0, 1, s);
+  if (st) return st;
+  return hif4x_gemm(0, 0, n2, n1, n2, -1.0f, A22, ld, 0, work, n1, 0, 0.0f, A21, ld, 0, 1, s);
+}
+
+extern "C" int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
+                                    int *info_dev, void *stream) {
+  if (n <= 0 || batch <= 0 || !H || !U || !work || !info_dev) return HIF4X_ERR_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t nn = n * n;
+  if (cudaMemsetAsync(info_dev, 0, sizeof(int), s) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+  // work: [nn] reversed matrix per batch element + [nn] scratch for trtri
+  for (int64_t b = 0; b < batch; b++) {
+    float *P = work;
+    float *scratch = work + nn;
+    reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(H + b * nn, P, n, nn);
+    damp_diag_kernel<<<1, 1024, 0, s>>>(P, n, damp);
+    int st = potrf_lower(P, n, info_dev, s);
+    if (st) return st;
+    zero_upper_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, n, nn);
+    st = trtri_lower(P, n, n, scratch, s);
+    if (st) return st;
+    reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, U + b * nn, n, nn);
+  }
+  HIF4X_CHECK_LAUNCH();
+  int info = 0;
+  if (cudaMemcpyAsync(&info, info_dev, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return HIF4X_ERR_LAUNCH;
+  return info ? HIF4X_NOT_PD : HIF4X_OK;
+}
+
+extern "C" int hif4x_gptq(const float *X, const float *unit, const float *U, int64_t R, int64_t C, int64_t batch,
+                          int64_t u_batch_stride, float *Q, float *work, void *stream) {
+  if (R < 0 || C <= 0 || batch <= 0) return HIF4X_ERR_ARG;
+  if (R == 0) return HIF4X_OK;
+  if (!X || !unit || !U || !Q || !work) return HIF4X_ERR_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  // work: W (batch*R*C) followed by E (batch*R*128)
+  float *W = work;
+  float *E = work + batch * R * C;
+  if (cudaMemcpyAsync(W, X, sizeof(float) * batch * R * C, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return HIF4X_ERR_LAUNCH;
+  const size_t smem = sizeof(float) * (GQ_BLK * GQ_BLK + GQ_BLK * GQ_THREADS);
+  if (cudaFuncSetAttribute(gptq_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return HIF4X_ERR_LAUNCH;
+  for (int64_t i1 = 0; i1 < C; i1 += GQ_BLK) {
+    const int nb = (int)std::min<int64_t>(GQ_BLK, C - i1);
+    dim3 grid(nblk(R, GQ_THREADS), (unsigned)batch);
+    gptq_block_kernel<<<grid, GQ_THREADS, smem, s>>>(W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
+    HIF4X_CHECK_LAUNCH();
+    const int64_t i2 = i1 + nb;
+    if (i2 < C) {
+      // W[:, i2:] -= E1 @ U[i1:i2, i2:]
+      int st = hif4x_gemm(0, 0, R, C - i2, nb, -1.0f, E, GQ_BLK, R * GQ_BLK, U + i1 * C + i2, C, u_batch_stride,
+                          1.0f, W + i2, C, R * C, batch, s);
+      if (st) return st;
+    }
+  }
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_refine_rows(float *M, float *v4, const float *d, const float *G, int64_t T, int64_t C,
+                                 int rounds, int *flips, void *stream) {
+  if (T < 0 || C <= 0 || rounds < 0) return HIF4X_ERR_ARG;
+  if (T == 0 || rounds == 0) return HIF4X_OK;
+  if (!M || !v4 || !d || !G) return HIF4X_ERR_ARG;
+  int threads = (int)((C + RC - 1) / RC);
+  threads = ((threads + 31) / 32) * 32;
+  if (threads > 1024) return HIF4X_ERR_UNSUPPORTED;  // C > 8192
+  if (T > 0x7fffffff) return HIF4X_ERR_ARG;
+  refine_rows_kernel<<<(unsigned)T, threads, 0, (cudaStream_t)stream>>>(M, v4, d, G, T, C, rounds, flips);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}

@@ -61,6 +61,26 @@ SIGNATURES: dict[str, list] = {
     "hif4x_unit_flat": [vp, vp, vp, i64, i64, vp, vp],
     "hif4x_pack_dict5": [vp, vp, vp, vp, vp, i64, i64, vp, vp, vp],
     "hif4x_unpack_dict5": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp],
+    "hif4x_gemm": [i32, i32, i64, i64, i64, f32, vp, i64, i64, vp, i64, i64, f32, vp, i64, i64, i64, vp],
+    "hif4x_chol_upper_inv": [vp, i64, i64, f32, vp, vp, vp, vp],
+    "hif4x_gptq": [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp],
+    "hif4x_refine_rows": [vp, vp, vp, vp, i64, i64, i32, vp, vp],
+    "hif4x_col_abs_sum": [vp, i64, i64, vp, i32, vp, vp],
+    "hif4x_smooth_logm": [vp, i64, i64, vp, vp],
+    "hif4x_exp_scale": [vp, i64, f32, vp, vp],
+    "hif4x_gather_rows": [vp, vp, i64, i64, vp, vp],
+    "hif4x_gather_cols": [vp, vp, i64, i64, vp, vp],
+    "hif4x_scatter_cols": [vp, vp, i64, i64, vp, vp],
+    "hif4x_permute_sym": [vp, vp, i64, vp, vp],
+    "hif4x_scale_cols": [vp, vp, i64, i64, i32, vp, vp],
+    "hif4x_reduce": [vp, vp, i64, i32, vp, vp, vp],
+    "hif4x_diag": [vp, i64, vp, vp],
+    "hif4x_argsort_desc": [vp, i64, vp, vp],
+    "hif4x_cast": [vp, i32, vp, i32, i64, vp],
+    "hif4x_refine_prep": [vp, vp, i64, vp, vp, vp],
+    "hif4x_axpby": [vp, vp, vp, f32, i64, vp, vp],
+    "hif4x_attention": [vp, vp, vp, i64, i32, i32, i32, vp, vp],
+    "hif4x_heads_transpose": [vp, i64, i64, i64, i32, vp, vp],
 }
 
 _LIB = None

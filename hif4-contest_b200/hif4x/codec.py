@@ -64,10 +64,12 @@ _SIGN_CACHE: dict = {}
 
 
 def rot_signs_host(n_vec: int, length: int = 64, seed0: int = 777) -> np.ndarray:
-    out = np.empty(max(n_vec, 1), np.uint64)
+    """Sign masks (n_vec words for length <= 64, else n_vec * ceil(length/64))."""
+    words = (length + 63) // 64
+    out = np.empty(max(n_vec * words, 1), np.uint64)
     L.call("hif4x_rot_signs", L.i64(n_vec), L.i64(length), ctypes.c_uint32(seed0),
            out.ctypes.data_as(ctypes.c_void_p))
-    return out[:n_vec]
+    return out[:n_vec * words]
 
 
 def rot_signs(nb: int, device) -> torch.Tensor:

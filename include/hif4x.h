@@ -108,15 +108,15 @@ int hif4x_nvfp4_decode_packed(const uint8_t *codes, const uint8_t *e4m3, float s
                               int64_t cols, void *out, int out_dtype, void *stream);
 
 /* _rot_blocks (example/solution/solution.py:222-245): bit-exact with the
- * reference's fp32 einsum.  signs may be NULL (then the reference's seeded
- * signs for block b = 0..cols/64-1 are used from a library-owned table). */
+ * reference's fp32 einsum.  signs: device table of cols/64 masks from
+ * hif4x_rot_signs (seed0 777). */
 int hif4x_rotate64(const float *x, const uint64_t *signs, int64_t rows, int64_t cols, float *out,
                    void *stream);
 
-/* Host: the reference's rotation sign masks.  Bit e of out[b] is set when
- * torch.Generator().manual_seed(seed0 + b) draws rand(len)[e] >= 0.5, i.e.
- * sign -1 (solution.py:240-242 with seed0 777, len 64; solution.py:1114-1115
- * with seed0 0xA5A5 + dh, len dh <= 64 per word). */
+/* Host: the reference's rotation sign masks.  Vector b (ceil(len/64) words)
+ * has bit e set when torch.Generator().manual_seed(seed0 + b) draws
+ * rand(len)[e] >= 0.5, i.e. sign -1 (solution.py:240-242 with seed0 777,
+ * len 64; _make_R, solution.py:1114-1115, with seed0 0xA5A5 + dh, len dh). */
 int hif4x_rot_signs(int64_t n_vec, int64_t len, uint32_t seed0, uint64_t *out_host);
 
 /* _quantize_weighted(x, ones) (example/solution/solution.py:744-770) on fp32
@@ -155,6 +155,84 @@ int hif4x_pack_dict5(const float *sf, const float *lv2, const float *lv3, const 
                      void *stream);
 int hif4x_unpack_dict5(const uint32_t *meta, const uint8_t *codes, int64_t rows, int64_t cols,
                        float *sf, float *lv2, float *lv3, float *sign, float *mant, void *stream);
+
+
+/* ---- calibration pipeline: linear algebra (csrc/linalg.cu) ------------- */
+
+/* Strided-batched fp32 GEMM, row-major:  C = alpha * op(A) op(B) + beta * C,
+ * op(A) = A (M x K, lda) or A^T (A stored K x M) when ta; same for B.
+ * Replaces every fp32 `@` / torch.matmul / einsum of the calibration path
+ * (e.g. example/solution/solution.py:860, 868, 894, 906, 928-931, 941, 1011-1012). */
+int hif4x_gemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+               int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C, int64_t ldc,
+               int64_t strideC, int64_t batch, void *stream);
+
+/* _upper_cholesky_inv (example/solution/solution.py:287-300): U upper with
+ * U^T U = (H + damp * max(mean(diag H), 1e-30) I)^-1, for `batch` n x n
+ * matrices.  Computed as one Cholesky of the index-reversed matrix and one
+ * triangular inverse (U = J L^-1 J with J H J = L L^T).  Synchronises the
+ * stream; returns HIF4X_NOT_PD (U undefined) where the reference's torch
+ * Cholesky would raise.  work: 2*n*n floats; info_dev: one device int. */
+int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
+                         int *info_dev, void *stream);
+
+/* _gptq_quantize_values / _gptq_quantize_batched (example/solution/
+ * solution.py:303-425): column-sequential GPTQ over the last axis in blocks of
+ * 128 with lazy trailing updates.  X, unit, Q: batch x R x C; U: C x C with
+ * batch stride u_batch_stride (0 = shared).  work: batch*R*(C+128) floats. */
+int hif4x_gptq(const float *X, const float *unit, const float *U, int64_t R, int64_t C, int64_t batch,
+               int64_t u_batch_stride, float *Q, float *work, void *stream);
+
+/* _rounds_active / _rounds_np (example/solution/solution.py:474-618): greedy
+ * top-1 flips per row for `rounds` rounds against the Gram G (C x C); M, v4
+ * (T x C) updated in place, d = 0.25*unit.  C <= 8192.  flips (T ints, may be
+ * NULL) receives the flip count per row. */
+int hif4x_refine_rows(float *M, float *v4, const float *d, const float *G, int64_t T, int64_t C, int rounds,
+                      int *flips, void *stream);
+
+/* ---- calibration pipeline: helpers (csrc/util.cu) ---------------------- */
+
+/* out[c] (+)= sum_r |X[r][c]| (solution.py:850).  work: 64*C floats. */
+int hif4x_col_abs_sum(const float *X, int64_t R, int64_t C, float *out, int accumulate, float *work,
+                      void *stream);
+/* logm = log(max(abs_sum/n_tok, 1e-12)) centred (solution.py:855-857). */
+int hif4x_smooth_logm(const float *abs_sum, int64_t C, int64_t n_tok, float *logm, void *stream);
+/* s = exp(alpha * logm) (solution.py:864, 871). */
+int hif4x_exp_scale(const float *logm, int64_t C, float alpha, float *s, void *stream);
+/* dst = src[idx] (rows), dst = src[:, idx], dst[:, idx] = src, out = A[idx][:, idx]
+ * (solution.py:858-859, 946, 958-967, 1060-1064). */
+int hif4x_gather_rows(const float *src, const int64_t *idx, int64_t n, int64_t C, float *dst, void *stream);
+int hif4x_gather_cols(const float *src, const int64_t *idx, int64_t R, int64_t C, float *dst, void *stream);
+int hif4x_scatter_cols(const float *src, const int64_t *idx, int64_t R, int64_t C, float *dst, void *stream);
+int hif4x_permute_sym(const float *A, const int64_t *idx, int64_t n, float *out, void *stream);
+/* out = X * s[c] or X / s[c] (solution.py:865-873, 1049). */
+int hif4x_scale_cols(const float *X, const float *s, int64_t R, int64_t C, int mode, float *out, void *stream);
+/* op 0: sum((A - B)^2), op 1: sum(|A|), double result (the guards' MSEs,
+ * solution.py:868, 906, 930-931; the weight hash, solution.py:995).
+ * work: 1024 doubles. */
+int hif4x_reduce(const float *A, const float *B, int64_t n, int op, double *out, double *work, void *stream);
+/* out[i] = A[i][i] */
+int hif4x_diag(const float *A, int64_t n, float *out, void *stream);
+/* torch.argsort(v, descending=True) (solution.py:945); ties by index; n <= 16384. */
+int hif4x_argsort_desc(const float *v, int64_t n, int64_t *idx, void *stream);
+/* fp32 <-> bf16 (solution.py:1011-1012, 1077). */
+int hif4x_cast(const void *in, int in_dtype, void *out, int out_dtype, int64_t n, void *stream);
+/* v4 = round(values/unit*4), d = unit/4 (solution.py:634-635). */
+int hif4x_refine_prep(const float *values, const float *unit, int64_t n, float *v4, float *d, void *stream);
+/* out = a*b + alpha*c elementwise (b, c may be NULL). */
+int hif4x_axpby(const float *a, const float *b, const float *c, float alpha, int64_t n, float *out, void *stream);
+
+/* ---- attention path (csrc/attention.cu) -------------------------------- */
+
+/* _attention_out / attn_ref (example/solution/solution.py:1247-1258,
+ * dev/hif4.py:59-71): fp32 GQA softmax(Q K^T / sqrt(dh)) V, non-causal.
+ * Q, O: (T, qh*dh); K, V: (T, kvh*dh); dh <= 128. */
+int hif4x_attention(const float *Q, const float *K, const float *V, int64_t T, int qh, int kvh, int dh, float *O,
+                    void *stream);
+
+/* (T, H, D) -> (H, T, D) (inverse = 0) or back (inverse = 1); the head
+ * permutes of solution.py:1217-1225, 1353-1361. */
+int hif4x_heads_transpose(const float *in, int64_t T, int64_t H, int64_t D, int inverse, float *out, void *stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,103 @@
+"""Seeded pipeline cases shared by the golden generator and the GPU tests.
+
+Inputs are rebuilt from seeds with torch's CPU generator (deterministic for
+a given torch version); the golden file stores a sha256 of the packed NVFP4
+bytes so a divergent generator is detected instead of silently compared.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "..", "..", "hif4-contest_b200"))
+from hif4x import synth  # noqa: E402
+
+# name: (N, C, calib rows, test rows, seed)
+LINEAR_CASES = {
+    "lin_c1024": (256, 1024, (192, 192, 192, 192), (16, 160, 400), 101),
+    "lin_c2560": (192, 2560, (160, 160, 160), (48, 520), 202),
+    "lin_c4224": (128, 4224, (128, 128, 128), (96,), 303),
+}
+
+# name: (qh, kvh, dh, calib T list (last = hold-out), test T list, seed)
+ATTN_CASES = {
+    "attn_h8": (8, 2, 128, (256, 256, 256, 256), (256, 64), 404),
+}
+
+
+def _digest(h, packed):
+    for t in packed[:2]:
+        h.update(t.numpy().tobytes())
+    h.update(np.float32(packed[2]).tobytes())
+
+
+def linear_inputs(name: str):
+    """Returns (weight pair, calib pairs, test pairs, sha256 hex)."""
+    N, C, calib_rows, test_rows, seed = LINEAR_CASES[name]
+    h = hashlib.sha256()
+    w = synth.weight_c0(seed, N, C)
+    pw = synth.quantize_nvfp4(w)
+    _digest(h, pw)
+    calib, tests = [], []
+    for i, T in enumerate(calib_rows):
+        p = synth.quantize_nvfp4(synth.acts_outlier(seed * 10 + i, T, C, n_out=max(2, C // 512)))
+        _digest(h, p)
+        calib.append(list(synth.reference_form(*p)))
+    for i, T in enumerate(test_rows):
+        p = synth.quantize_nvfp4(synth.acts_outlier(seed * 10 + 50 + i, T, C, n_out=max(2, C // 512)))
+        _digest(h, p)
+        tests.append(list(synth.reference_form(*p)))
+    return list(synth.reference_form(*pw)), calib, tests, h.hexdigest()
+
+
+def attn_inputs(name: str):
+    qh, kvh, dh, calib_T, test_T, seed = ATTN_CASES[name]
+    h = hashlib.sha256()
+
+    def sample(s, T):
+        g = torch.Generator().manual_seed(s)
+        q = (torch.randn(T, qh * dh, generator=g)).to(torch.bfloat16)
+        k = synth.kv_rope(s + 1, T, kvh, dh)
+        v = (torch.randn(T, kvh * dh, generator=g)).to(torch.bfloat16)
+        out = {}
+        for role, x in (("q", q), ("k", k), ("v", v)):
+            p = synth.quantize_nvfp4(x)
+            _digest(h, p)
+            out[role] = list(synth.reference_form(*p))
+        return out
+
+    calib = [sample(seed * 10 + i, T) for i, T in enumerate(calib_T)]
+    tests = [sample(seed * 10 + 50 + i, T) for i, T in enumerate(test_T)]
+    return (qh, kvh, dh), calib, tests, h.hexdigest()
+
+
+def deq_nvfp4(pair) -> torch.Tensor:
+    q, s = pair
+    return (q.float().unflatten(-1, (-1, 16)) * s.float().unsqueeze(-1)).flatten(-2, -1).to(torch.bfloat16).float()
+
+
+def deq_dict5(p: dict) -> torch.Tensor:
+    v = p["sign"] * p["mant"] * p["scale_lv3"] * p["scale_lv2"] * p["scale_factor"]
+    return v.flatten(-4, -1).float()
+
+
+def alg1(x: torch.Tensor) -> dict:
+    """Algorithm 1 (dev/variants.py:249-287) through the C oracle."""
+    sys.path.insert(0, os.path.join(HERE, "..", "..", "oracle"))
+    import oracle
+    p = oracle.encode_alg1(x.float().numpy())
+    return {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in p.items()}
+
+
+def attn_ref(q, k, v, qh, kvh, dh):
+    seq = q.shape[0]
+    qf = q.float().view(seq, qh, dh).transpose(0, 1)
+    kf = k.float().view(seq, kvh, dh).transpose(0, 1).repeat_interleave(qh // kvh, dim=0)
+    vf = v.float().view(seq, kvh, dh).transpose(0, 1).repeat_interleave(qh // kvh, dim=0)
+    prob = torch.softmax(torch.bmm(qf, kf.transpose(1, 2)) / (dh ** 0.5), dim=-1)
+    return torch.bmm(prob, vf).transpose(0, 1).reshape(seq, qh * dh)

@@ -1,0 +1,164 @@
+"""GPU numerics of the calibration kernels against plain torch fp32/fp64
+references and the numpy restatement in oracle/pipeline_oracle.py."""
+import numpy as np
+import pytest
+import torch
+
+import pipeline_oracle as po
+
+pytestmark = pytest.mark.gpu
+
+from hif4x import _lib as L  # noqa: E402
+from hif4x import attention as att  # noqa: E402
+from hif4x import codec  # noqa: E402
+from hif4x import linalg as la  # noqa: E402
+
+
+def rnd(*shape, seed=0, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).cuda()
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (130, 77, 9), (257, 300, 1000), (64, 128, 4096)])
+def test_gemm_vs_torch(ta, tb, M, N, K):
+    A = rnd(K, M, seed=1) if ta else rnd(M, K, seed=1)
+    B = rnd(N, K, seed=2) if tb else rnd(K, N, seed=2)
+    ref = (A.double().T if ta else A.double()) @ (B.double().T if tb else B.double())
+    got = la.gemm(A, B, ta=bool(ta), tb=bool(tb))
+    tol = 2e-6 * np.sqrt(K) * float(ref.abs().max()) + 1e-6
+    assert float((got.double() - ref).abs().max()) <= tol
+
+
+def test_gemm_accumulate_strided_batched():
+    A = rnd(3, 40, 50, seed=3)
+    B = rnd(50, 60, seed=4)
+    C = rnd(3, 40, 60, seed=5)
+    ref = 0.5 * (A.double() @ B.double()) + 2.0 * C.double()
+    got = la.gemm_batched(A, B, alpha=0.5, beta=2.0, out=C.clone())
+    assert torch.allclose(got.double(), ref, atol=1e-4, rtol=1e-5)
+
+
+@pytest.mark.parametrize("n", [64, 100, 256, 1000])
+def test_chol_upper_inv(n):
+    X = rnd(3 * n, n, seed=n)
+    H = X.T @ X
+    U = la.chol_upper_inv(H)
+    assert U is not None
+    Uh = U.double().cpu()
+    assert torch.equal(Uh, torch.triu(Uh))
+    Hd = H.double().cpu()
+    Hd = Hd + torch.eye(n, dtype=torch.float64) * max(float(Hd.diagonal().mean()), 1e-30) * 0.1
+    err = (Uh.T @ Uh @ Hd - torch.eye(n, dtype=torch.float64)).abs().max()
+    assert float(err) < 1e-3
+    Uref = torch.from_numpy(po.upper_cholesky_inv(H.cpu().numpy())).double()
+    assert float((Uh - Uref).abs().max() / Uref.abs().max()) < 1e-3
+
+
+def test_chol_batched_and_not_pd():
+    Hb = torch.stack([rnd(300, 64, seed=s).T @ rnd(300, 64, seed=s) for s in range(3)])
+    Ub = la.chol_upper_inv(Hb)
+    for b in range(3):
+        assert torch.allclose(Ub[b], la.chol_upper_inv(Hb[b].contiguous()), atol=1e-5, rtol=1e-4)
+    # host-side failure injection: an indefinite matrix takes the reference's skip branch
+    bad = -torch.eye(64, device="cuda")
+    assert la.chol_upper_inv(bad) is None
+
+
+@pytest.mark.parametrize("R,C", [(33, 128), (300, 384), (256, 1000 // 64 * 64)])
+def test_gptq_vs_oracle(R, C):
+    X = rnd(R, C, seed=7, scale=0.05)
+    Hx = rnd(2 * C, C, seed=8)
+    U = la.chol_upper_inv(Hx.T @ Hx)
+    unit = codec.unit_flat(codec.encode(X))
+    got = la.gptq(X, unit, U).cpu().numpy()
+    want = po.gptq(X.cpu().numpy(), unit.cpu().numpy(), U.cpu().numpy())
+    mism = np.mean(got != want)
+    assert mism < 0.01, mism
+    # values lie on each element's unit grid
+    u = unit.cpu().numpy()
+    m4 = np.abs(got) / u * 4
+    assert np.all(m4 == np.round(m4)) and np.all(m4 <= 7)
+
+
+def test_gptq_batched_matches_loop():
+    Xb = rnd(4, 70, 128, seed=9, scale=0.1)
+    Ub = torch.stack([la.chol_upper_inv((lambda A: A.T @ A)(rnd(256, 128, seed=20 + i))) for i in range(4)])
+    units = torch.stack([codec.unit_flat(codec.encode(Xb[i].contiguous())) for i in range(4)])
+    got = la.gptq(Xb, units, Ub)
+    for i in range(4):
+        assert torch.equal(got[i], la.gptq(Xb[i].contiguous(), units[i].contiguous(), Ub[i].contiguous()))
+
+
+@pytest.mark.parametrize("T,C", [(5, 256), (64, 1024), (40, 2048)])
+def test_refine_rows_vs_oracle(T, C):
+    X = rnd(T, C, seed=11)
+    Wq = rnd(256, C, seed=12, scale=0.05)
+    G = Wq.T @ Wq
+    p = codec.encode(X)
+    unit = codec.unit_flat(p)
+    vals = codec.decode(p)
+    v4, d = la.refine_prep(vals, unit)
+    M = la.gemm(la.mul(v4, d), G)
+    la.gemm(X, G, alpha=-1.0, beta=1.0, out=M)
+    Mo, v4o, fo = po.refine_rounds(M.cpu().numpy().copy(), v4.cpu().numpy().copy(), d.cpu().numpy(),
+                                   G.cpu().numpy(), 200)
+    flips = la.refine_rows(M, v4, d, G, 200).cpu().numpy()
+    # identical flip sequences except where fp32 rounding of M ties differently
+    assert np.mean(v4.cpu().numpy() != v4o) < 0.02
+    assert abs(int(flips.sum()) - int(fo.sum())) <= max(3, 0.05 * fo.sum())
+    # the objective decreased: ||(v4 d) - x|| in the G metric
+    e0 = ((vals - X) @ G * (vals - X)).sum()
+    w1 = la.mul(v4, d)
+    e1 = ((w1 - X) @ G * (w1 - X)).sum()
+    assert float(e1) <= float(e0)
+
+
+def test_attention_vs_torch():
+    T, qh, kvh, dh = 200, 8, 2, 128
+    q, k, v = rnd(T, qh * dh, seed=1), rnd(T, kvh * dh, seed=2), rnd(T, kvh * dh, seed=3)
+    got = att.attention_out(q, k, v, qh, kvh, dh)
+    qf = q.double().view(T, qh, dh).transpose(0, 1)
+    kf = k.double().view(T, kvh, dh).transpose(0, 1).repeat_interleave(4, 0)
+    vf = v.double().view(T, kvh, dh).transpose(0, 1).repeat_interleave(4, 0)
+    ref = (torch.softmax(qf @ kf.transpose(1, 2) / dh ** 0.5, -1) @ vf).transpose(0, 1).reshape(T, -1)
+    assert float((got.double() - ref).abs().max()) < 1e-4
+
+
+def test_helpers_vs_torch():
+    X = rnd(1000, 320, seed=5)
+    out = torch.zeros(320, device="cuda")
+    la.col_abs_sum(X, out)
+    assert torch.allclose(out, X.abs().sum(0), rtol=1e-5)
+    logm = la.smooth_logm(out, 1000)
+    m = (out / 1000).clamp_min(1e-12).log()
+    assert torch.allclose(logm, m - m.mean(), atol=1e-5)
+    assert torch.allclose(la.exp_scale(logm, 0.3), torch.exp(logm * 0.3), rtol=1e-6)
+    v = torch.randn(3000, device="cuda")
+    v[5] = v[9]
+    idx = la.argsort_desc(v)
+    assert torch.equal(v[idx], torch.sort(v, descending=True).values)
+    perm = torch.randperm(320).cuda()
+    assert torch.equal(la.gather_cols(X, perm), X[:, perm])
+    assert torch.equal(la.scatter_cols(la.gather_cols(X, perm), perm), X)
+    A = rnd(50, 50, seed=6)
+    p50 = torch.randperm(50).cuda()
+    assert torch.equal(la.permute_sym(A, p50), A[p50][:, p50])
+    assert abs(la.mse(X, X * 0.5) - float(((X * 0.5) ** 2).double().mean())) < 1e-9
+    assert abs(la.abs_sum_f64(X) - float(X.double().abs().sum())) < 1e-6
+    xt = att.heads_first(rnd(10, 4 * 16, seed=1), 4)
+    assert torch.equal(att.heads_last(xt), xt.permute(1, 0, 2).reshape(10, 64))
+    b = la.to_bf16(X)
+    assert torch.equal(b, X.bfloat16()) and torch.equal(la.to_f32(b), X.bfloat16().float())
+
+
+def test_make_R_matches_reference_construction():
+    dh = 128
+    H = torch.tensor([[1.0]])
+    while H.shape[0] < dh:
+        H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)], 0)
+    H = H / (dh ** 0.5)
+    g = torch.Generator().manual_seed(0xA5A5 + dh)
+    d = (torch.rand(dh, generator=g) < 0.5).float() * 2 - 1
+    assert torch.equal(att.make_R(dh, "cuda").cpu(), H * d.unsqueeze(0))
+    assert att.make_R(96, "cuda") is None
