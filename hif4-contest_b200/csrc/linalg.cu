@@ -540,3 +540,85 @@ extern "C" int hif4x_refine_rows(float *M, float *v4, const float *d, const floa
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
 }
+
+// ====================================================================== no-allocation variant
+// hif4x_chol_upper_inv_noalloc: the same damped Cholesky -> upper factor of
+// the inverse, for callers that cannot allocate device memory at the call
+// (a host whose device memory is planned up front by another runtime, or a
+// latency-bound loop that must not call the allocator, which can synchronise
+// the device).  Its scratch is a file-scope device array of fixed size, so
+// it takes no work or info buffers: n is limited to kNoAllocMaxN.
+//
+// Host code cannot pass the array's name to a kernel (in host code that name
+// is a host-side stand-in, not a device address), so the first call on each
+// device resolves the device address with cudaGetSymbolAddress while that
+// device is current and caches it; make that first call before any stream
+// capture.  All calls share the one array: calls that overlap on the GPU
+// (different streams or host threads at once) race on it.
+#include <mutex>
+
+namespace {
+constexpr int64_t kNoAllocMaxN = 512;
+constexpr int kNoAllocMaxDevices = 64;
+// [0, n*n): index-reversed damped matrix, later L and L^-1; [n*n, 2*n*n): trtri work
+static __device__ __align__(256) float g_chol_noalloc_scratch[2 * kNoAllocMaxN * kNoAllocMaxN];
+// [0]: non-positive-pivot flag (cleared at the start of every call)
+static __device__ __align__(256) int g_chol_noalloc_info[64];
+
+struct NoAllocPtrs {
+  float *scratch;
+  int *info;
+  bool ready;
+};
+NoAllocPtrs g_noalloc_ptrs[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+int noalloc_device_ptrs(float **scratch, int **info) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return HIF4X_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocPtrs &p = g_noalloc_ptrs[dev];
+  if (!p.ready) {
+    void *s = nullptr, *i = nullptr;
+    if (cudaGetSymbolAddress(&s, g_chol_noalloc_scratch) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+    if (cudaGetSymbolAddress(&i, g_chol_noalloc_info) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+    p.scratch = static_cast<float *>(s);
+    p.info = static_cast<int *>(i);
+    p.ready = true;
+  }
+  *scratch = p.scratch;
+  *info = p.info;
+  return HIF4X_OK;
+}
+}  // namespace
+
+extern "C" int hif4x_chol_upper_inv_noalloc(const float *H, int64_t n, int64_t batch, float damp, float *U,
+                                            void *stream) {
+  if (n <= 0 || batch <= 0 || !H || !U) return HIF4X_ERR_ARG;
+  if (n > kNoAllocMaxN) return HIF4X_ERR_SCRATCH;
+  float *scratch = nullptr;
+  int *info_dev = nullptr;
+  int st = noalloc_device_ptrs(&scratch, &info_dev);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t nn = n * n;
+  if (cudaMemsetAsync(info_dev, 0, sizeof(int), s) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+  for (int64_t b = 0; b < batch; b++) {
+    float *P = scratch;
+    float *work = scratch + nn;
+    reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(H + b * nn, P, n, nn);
+    damp_diag_kernel<<<1, 1024, 0, s>>>(P, n, damp);
+    st = potrf_lower(P, n, info_dev, s);
+    if (st) return st;
+    zero_upper_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, n, nn);
+    st = trtri_lower(P, n, n, work, s);
+    if (st) return st;
+    reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, U + b * nn, n, nn);
+  }
+  HIF4X_CHECK_LAUNCH();
+  int info = 0;
+  if (cudaMemcpyAsync(&info, info_dev, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return HIF4X_ERR_LAUNCH;
+  return info ? HIF4X_NOT_PD : HIF4X_OK;
+}

@@ -15,14 +15,15 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 SO_PATH = os.path.join(_HERE, "libhif4x.so")
 
 OK, NOT_PD, TIMEOUT = 0, 1, 2
-ERR_ARG, ERR_LAUNCH, ERR_UNSUPPORTED = -1, -2, -3
+ERR_ARG, ERR_LAUNCH, ERR_UNSUPPORTED, ERR_SCRATCH = -1, -2, -3, -4
 DT_F32, DT_BF16 = 0, 1
 SRC_NVFP4_PACKED, SRC_NVFP4_PAIR, SRC_VALUES = 0, 1, 2
 SMOOTH_NONE, SMOOTH_MUL, SMOOTH_DIV = 0, 1, 2
 ENC_NONE, ENC_SEARCH, ENC_FAST, ENC_ALG1 = 0, 1, 2, 3
 
 _STATUS = {OK: "ok", NOT_PD: "not positive definite", TIMEOUT: "device wait timed out",
-           ERR_ARG: "bad argument", ERR_LAUNCH: "CUDA launch error", ERR_UNSUPPORTED: "unsupported"}
+           ERR_ARG: "bad argument", ERR_LAUNCH: "CUDA launch error", ERR_UNSUPPORTED: "unsupported",
+           ERR_SCRATCH: "size above the static scratch maximum"}
 
 
 class Hif4xError(RuntimeError):
@@ -81,6 +82,7 @@ SIGNATURES: dict[str, list] = {
     "hif4x_axpby": [vp, vp, vp, f32, i64, vp, vp],
     "hif4x_attention": [vp, vp, vp, i64, i32, i32, i32, vp, vp],
     "hif4x_heads_transpose": [vp, i64, i64, i64, i32, vp, vp],
+    "hif4x_chol_upper_inv_noalloc": [vp, i64, i64, f32, vp, vp],
 }
 
 _LIB = None

@@ -42,6 +42,7 @@ extern "C" {
 #define HIF4X_ERR_ARG (-1)        /* bad pointer / size / alignment           */
 #define HIF4X_ERR_LAUNCH (-2)     /* CUDA launch or runtime error             */
 #define HIF4X_ERR_UNSUPPORTED (-3)
+#define HIF4X_ERR_SCRATCH (-4)    /* size above a static scratch maximum      */
 
 /* ---- enums ------------------------------------------------------------- */
 #define HIF4X_DT_F32 0
@@ -175,6 +176,20 @@ int hif4x_gemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, con
  * Cholesky would raise.  work: 2*n*n floats; info_dev: one device int. */
 int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
                          int *info_dev, void *stream);
+
+/* Allocation-free twin of hif4x_chol_upper_inv (no counterpart in the
+ * reference).  For callers that cannot allocate device memory at the call --
+ * a host whose device memory another runtime plans up front, or a
+ * latency-bound loop that must not call the allocator (which can synchronise
+ * the device) -- it takes no work or info buffers: its scratch is a static
+ * device array of 2*512*512 floats (2 MiB, held by every GPU that loads the
+ * library until exit), so n <= 512; larger n returns HIF4X_ERR_SCRATCH.
+ * The first call on a device, with that device current, looks up the array's
+ * device address (cudaGetSymbolAddress) and caches it: make that first call
+ * before any stream capture.  All calls share the one array and each call
+ * clears the pivot flag it needs; calls that overlap on the GPU race.  Same
+ * results and status codes as hif4x_chol_upper_inv; synchronises the stream. */
+int hif4x_chol_upper_inv_noalloc(const float *H, int64_t n, int64_t batch, float damp, float *U, void *stream);
 
 /* _gptq_quantize_values / _gptq_quantize_batched (example/solution/
  * solution.py:303-425): column-sequential GPTQ over the last axis in blocks of
