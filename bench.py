@@ -22,6 +22,7 @@ import subprocess
 import sys
 import threading
 import time
+import zlib
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "hif4-contest_b200"))
@@ -316,6 +317,97 @@ def e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dis
     return e2e_ms, launches_e2e, int(codes_h.numel() + e4m3_h.numel()), int(meta_h.numel() * 4 + hcodes_h.numel())
 
 
+def run_layer(args, rank, ws, local_rank):
+    """Pipeline workload: Llama-3-8B-shaped decoder layers (7 matrices each),
+    full calibration (smoothing, rotation choice, GPTQ, refinement, Gram
+    carries) plus one 1024-token dynamic activation call per matrix, through
+    the public API with CPU tensors.  Whole matrices are sharded over the
+    ranks by LPT; the packed HiF4 weights are gathered to rank 0 (NCCL).
+    value = matrices/s over all ranks (fixed total work: strong scaling)."""
+    import torch
+
+    from hif4x import linear, shard, synth
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+    T_cal, n_cal, T_test = 4096, 4, 1024
+    jobs = shard.model_jobs(args.layers)
+    mine = shard.rank_jobs(jobs, rank, ws, T_cal)
+
+    def pair(x):
+        return [t.cpu() for t in synth.reference_form(*synth.quantize_nvfp4(x))]
+
+    inputs = {}
+
+    def acts(layer, input_id, C, seed_off, T):
+        seed = 10_000 * layer + zlib.crc32(input_id.encode()) % 997 * 10 + seed_off
+        if input_id == "mlp_act":
+            return synth.acts_silu(seed, T, C, device=dev)
+        return synth.acts_outlier(seed, T, C, n_out=max(1, round(C * 0.002)), gain=20.0, device=dev)
+
+    for j in mine:
+        key = (j.layer, j.input_id)
+        if key not in inputs:
+            inputs[key] = ([pair(acts(j.layer, j.input_id, j.C, i, T_cal // n_cal)) for i in range(n_cal)],
+                           pair(acts(j.layer, j.input_id, j.C, 99, T_test)))
+    weights = {j.key: pair((torch.randn(j.N, j.C, device=dev,
+                                        generator=torch.Generator(device=dev).manual_seed(zlib.crc32(j.key.encode())))
+                            * 0.02).to(torch.bfloat16)) for j in mine}
+    torch.cuda.synchronize(dev)
+
+    packed = {}
+
+    def step():
+        for j in mine:
+            calib, test = inputs[(j.layer, j.input_id)]
+            wq, wsc = weights[j.key]
+            res = linear.calibrate_weight(wq, wsc, calib)
+            linear.dynamic_activation(test[0], test[1], res["activation_state"])
+            packed[j.key] = shard.pack_params(res["weight_params"])
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize(dev)
+    t1 = time.perf_counter()
+    dt = (t1 - t0) / max(args.steps, 1)
+    if dist is not None:
+        t = torch.tensor([dt], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t[0])
+        g0 = time.perf_counter()
+        shards = shard.gather_shards(packed, dist, dev)
+        torch.cuda.synchronize(dev)
+        gather_s = time.perf_counter() - g0
+    else:
+        shards, gather_s = packed, 0.0
+    if rank != 0:
+        return
+    elems = sum(j.N * j.C for j in jobs)
+    assert shards is not None and len(shards) == len(jobs)
+    print(json.dumps({
+        "metric": "NVFP4->HiF4 weight-set conversion, matrices/s (full calibration + one dynamic call each)",
+        "value": len(jobs) / dt, "unit": "matrices/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.layers} Llama-3-8B-shaped decoder layer(s), {len(jobs)} matrices, "
+                               f"{T_cal} calibration tokens per input ({n_cal} x {T_cal // n_cal}), 1 x {T_test} "
+                               "dynamic tokens per matrix", "parallelism": f"LPT over {ws} GPU(s)"},
+        "weight_gelem_per_s": elems / dt / 1e9, "gather_s": gather_s,
+        "wall_clock_note": "host wall clock around synchronised steps (the API returns CPU tensors)",
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -324,8 +416,10 @@ def main():
     ap.add_argument("--impl", default="hif4x", choices=["hif4x", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--workload", default="codec", choices=["codec", "layer"])
+    ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and args.workload == "codec":
         args.warmup = 3
     if args.impl == "reference":
         # rank 0 alone times the CPU reference; the other ranks exit at once
@@ -333,7 +427,10 @@ def main():
         return
     rank, ws, local_rank = dist_init()
     try:
-        run_gpu(args, rank, ws, local_rank)
+        if args.workload == "layer":
+            run_layer(args, rank, ws, local_rank)
+        else:
+            run_gpu(args, rank, ws, local_rank)
     finally:
         if ws > 1:
             import torch.distributed as dist

@@ -8,6 +8,7 @@
 // accumulation, so every product matches the reference's fp32 matmuls to
 // rounding.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -417,9 +418,42 @@ using namespace hif4x;
 
 static inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
 
+extern "C" int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
+                             int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
+                             void *stream);
+
+extern "C" int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
+                               int64_t lda, int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta,
+                               float *C, int64_t ldc, int64_t strideC, int64_t batch, void *stream);
+
+// Products of at least this many multiply-adds go to the tensor cores.
+static const int64_t kTcMinMacs = int64_t(1) << 26;
+
+static bool tc_disabled() {
+  static const bool off = [] {
+    const char *e = getenv("HIF4X_GEMM");
+    return e != nullptr && e[0] == 's';  // HIF4X_GEMM=simt selects the SIMT kernel for every product
+  }();
+  return off;
+}
+
 extern "C" int hif4x_gemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
                           int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
                           int64_t ldc, int64_t strideC, int64_t batch, void *stream) {
+  if (M < 0 || N < 0 || K < 0 || batch < 0) return HIF4X_ERR_ARG;
+  if (M == 0 || N == 0 || batch == 0) return HIF4X_OK;
+  if (!A || !B || !C || batch > 65535) return HIF4X_ERR_ARG;
+  if (batch == 1 && K >= 64 && M * N * K >= kTcMinMacs && !tc_disabled()) {
+    const int st = hif4x_gemm_tc(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, stream);
+    if (st != HIF4X_ERR_UNSUPPORTED) return st;
+  }
+  return hif4x_gemm_simt(ta, tb, M, N, K, alpha, A, lda, strideA, B, ldb, strideB, beta, C, ldc, strideC, batch,
+                         stream);
+}
+
+extern "C" int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
+                               int64_t lda, int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta,
+                               float *C, int64_t ldc, int64_t strideC, int64_t batch, void *stream) {
   if (M < 0 || N < 0 || K < 0 || batch < 0) return HIF4X_ERR_ARG;
   if (M == 0 || N == 0 || batch == 0) return HIF4X_OK;
   if (!A || !B || !C || batch > 65535) return HIF4X_ERR_ARG;

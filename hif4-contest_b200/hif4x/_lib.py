@@ -83,6 +83,9 @@ SIGNATURES: dict[str, list] = {
     "hif4x_attention": [vp, vp, vp, i64, i32, i32, i32, vp, vp],
     "hif4x_heads_transpose": [vp, i64, i64, i64, i32, vp, vp],
     "hif4x_chol_upper_inv_noalloc": [vp, i64, i64, f32, vp, vp],
+    "hif4x_gemm_tc": [i32, i32, i64, i64, i64, f32, vp, i64, vp, i64, f32, vp, i64, vp],
+    "hif4x_device_status": [vp],
+    "hif4x_gemm_simt": [i32, i32, i64, i64, i64, f32, vp, i64, i64, vp, i64, i64, f32, vp, i64, i64, i64, vp],
 }
 
 _LIB = None

@@ -159,6 +159,7 @@ def calibrate(calib_qkv_list: list, q_num_heads: int, kv_num_heads: int, head_di
             gq = 1
     if info is not None:
         info.update(rot=rot, gq=gq, T0=T0)
+    la.check_device_status(dev)
     q_state = {"rot": rot, "kvh": kvh}
     k_state = {"rot": rot, "kvh": kvh}
     if gq == 1:

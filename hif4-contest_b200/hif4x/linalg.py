@@ -19,9 +19,20 @@ def _s(t: torch.Tensor):
     return L.stream(t.device)
 
 
+def check_device_status(dev=None) -> None:
+    """Raise if a bounded device-side wait expired since the last check."""
+    st = L.lib().hif4x_device_status(L.stream(dev))
+    if st != L.OK:
+        raise L.Hif4xError("hif4x_device_status", st if st < 0 else -st)
+
+
 def gemm(A: torch.Tensor, B: torch.Tensor, *, ta: bool = False, tb: bool = False, alpha: float = 1.0,
-         beta: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
-    """out = alpha * op(A) @ op(B) + beta * out (2-D, row-major views with unit inner stride)."""
+         beta: float = 0.0, out: torch.Tensor | None = None, exact: bool = False) -> torch.Tensor:
+    """out = alpha * op(A) @ op(B) + beta * out (2-D, row-major views with unit inner stride).
+
+    Large products run on the tensor cores (3xTF32, fp32-faithful up to the
+    tensor core's truncating accumulation); exact=True keeps the product on
+    round-to-nearest fp32 FMAs, for results that get differenced."""
     M = A.shape[1] if ta else A.shape[0]
     K = A.shape[0] if ta else A.shape[1]
     N = B.shape[0] if tb else B.shape[1]
@@ -32,8 +43,8 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, ta: bool = False, tb: bool = False
         out = torch.empty(M, N, dtype=torch.float32, device=A.device)
         beta = 0.0
     assert out.stride(1) == 1
-    L.call("hif4x_gemm", int(ta), int(tb), M, N, K, L.f32(alpha), L.ptr(A), A.stride(0), 0, L.ptr(B),
-           B.stride(0), 0, L.f32(beta), L.ptr(out), out.stride(0), 0, 1, _s(A))
+    L.call("hif4x_gemm_simt" if exact else "hif4x_gemm", int(ta), int(tb), M, N, K, L.f32(alpha), L.ptr(A),
+           A.stride(0), 0, L.ptr(B), B.stride(0), 0, L.f32(beta), L.ptr(out), out.stride(0), 0, 1, _s(A))
     return out
 
 

@@ -66,6 +66,27 @@ def _search(x: torch.Tensor):
     return out["p"], out["deq"], out["unit"]
 
 
+class _Phases:
+    """Optional CUDA-event phase timer (enabled when the caller passes info)."""
+
+    def __init__(self, on: bool):
+        self.on = on
+        self.marks = []
+
+    def mark(self, name: str):
+        if self.on:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.marks.append((name, e))
+
+    def result(self) -> dict:
+        if not self.on or len(self.marks) < 2:
+            return {}
+        torch.cuda.synchronize()
+        return {self.marks[i + 1][0]: self.marks[i][1].elapsed_time(self.marks[i + 1][1])
+                for i in range(len(self.marks) - 1)}
+
+
 def _randperm(n: int, k: int, dev) -> torch.Tensor:
     """torch.randperm(n)[:k] on the host generator (the reference's RNG call)."""
     return torch.randperm(n)[:min(n, k)].to(dev)
@@ -94,13 +115,13 @@ def _refine_weight_values(w_final, q_used, weight_params: Dict5, calib_sm, mode)
     if rows == 0 or xh.shape[0] == 0:
         return weight_params, q_used
     A = la.gemm(la.sub(q_used, w_final), Gxx)          # (q - w_final) @ Gxx
-    ref_h = la.gemm(xh, w_final, tb=True)
-    hold0 = la.mse(la.gemm(xh, q_used, tb=True), ref_h)
+    ref_h = la.gemm(xh, w_final, tb=True, exact=True)
+    hold0 = la.mse(la.gemm(xh, q_used, tb=True, exact=True), ref_h)
     if not (0.0 < hold0 < float("inf")):
         return weight_params, q_used
     la.refine_rows(A, v4, d, Gxx, REFINE_W_SWEEPS * REFINE_ACT_ROUNDS)
     wn = la.mul(v4, d)
-    hold1 = la.mse(la.gemm(xh, wn, tb=True), ref_h)
+    hold1 = la.mse(la.gemm(xh, wn, tb=True, exact=True), ref_h)
     if hold1 < hold0:
         return codec.values_to_params(wn, weight_params), wn
     return weight_params, q_used
@@ -111,9 +132,12 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     """hif4_calibration_and_quantize_weight (solution.py:826-1026)."""
     torch.manual_seed(0)                                       # solution.py:838
     dev = _dev()
+    ph = _Phases(info is not None)
+    ph.mark("start")
     w = decode_pair((weight_quant, weight_scale), dev)
     R, C = w.shape
     acts_raw = [decode_pair(p, dev) for p in calib_activation_list]
+    ph.mark("upload_decode")
 
     # ---- alpha smoothing search (solution.py:844-873)
     abs_sum = torch.zeros(C, dtype=torch.float32, device=dev)
@@ -127,18 +151,19 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     logm = la.smooth_logm(abs_sum, n_tok)
     rows = _randperm(R, 256, dev)                              # solution.py:858
     w_rows = la.gather_rows(w, rows)
-    a_wr = la.gemm(a_big, w_rows, tb=True)
+    a_wr = la.gemm(a_big, w_rows, tb=True, exact=True)
     best_alpha, best_loss = 0.0, None
     for alpha in ALPHA_GRID:
         s = la.exp_scale(logm, alpha)
         wq = la.scale_cols(_encode_fast(w_rows, s)["deq"], s, L.SMOOTH_MUL)
-        loss = la.mse(la.gemm(a_big, wq, tb=True), a_wr)
+        loss = la.mse(la.gemm(a_big, wq, tb=True, exact=True), a_wr)
         if best_loss is None or loss < best_loss:
             best_loss, best_alpha = loss, alpha
     s = la.exp_scale(logm, best_alpha)
     w_s = la.scale_cols(w, s, L.SMOOTH_DIV)
     acts_s = [la.scale_cols(a, s, L.SMOOTH_MUL) for a in acts_raw]
     del acts_raw
+    ph.mark("alpha_search")
 
     # ---- transform choice {0: none, 1: rotation} (solution.py:875-911)
     mode, Uw, xh_pick = 0, None, None
@@ -163,7 +188,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
             pp = _encode_fast(w_rsub)
             qq = la.gptq(w_rsub, pp["unit"], U)
             xt = tf(xh_sub, md)
-            cand.append(la.mse(la.gemm(xt, qq, tb=True), la.gemm(xt, w_rsub, tb=True)))
+            cand.append(la.mse(la.gemm(xt, qq, tb=True, exact=True), la.gemm(xt, w_rsub, tb=True, exact=True)))
         mode = min(range(2), key=lambda i: (cand[i], i)) if not all(math.isnan(c) for c in cand) else 0
         if mode == 1 and spaces[1] is None:
             mode = 0
@@ -171,6 +196,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         spaces = None
         xh_pick = tf(xh_sub, mode)
 
+    ph.mark("transform_choice")
     w_final = tf(w_s, mode)
     ref_shared = None
     # ---- searched encode + hold-out-guarded GPTQ (solution.py:921-934)
@@ -178,15 +204,16 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     gptq_w = False
     if xh_pick is not None and Uw is not None:
         q_g = la.gptq(w_final, unit, Uw)
-        ref = la.gemm(xh_pick, w_final, tb=True)
+        ref = la.gemm(xh_pick, w_final, tb=True, exact=True)
         ref_shared = ref
-        mse_r = la.mse(la.gemm(xh_pick, q_used, tb=True), ref)
-        mse_g = la.mse(la.gemm(xh_pick, q_g, tb=True), ref)
+        mse_r = la.mse(la.gemm(xh_pick, q_used, tb=True, exact=True), ref)
+        mse_g = la.mse(la.gemm(xh_pick, q_g, tb=True, exact=True), ref)
         if mse_g < mse_r:
             weight_params = codec.values_to_params(q_g, weight_params)
             q_used = q_g
             gptq_w = True
     del Uw
+    ph.mark("weight_encode_gptq")
 
     # ---- activation-side GPTQ with act-order (solution.py:936-976)
     u_act, gptq_act, order = None, 0, None
@@ -204,15 +231,16 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
                 xg = la.scatter_cols(la.gptq(la.gather_cols(xh_pick, order), la.gather_cols(unit_x, order), Ua), order)
             else:
                 xg = la.gptq(xh_pick, unit_x, Ua)
-            ref2 = ref_shared if ref_shared is not None else la.gemm(xh_pick, w_final, tb=True)
-            mse_ar = la.mse(la.gemm(xr, q_used, tb=True), ref2)
-            mse_ag = la.mse(la.gemm(xg, q_used, tb=True), ref2)
+            ref2 = ref_shared if ref_shared is not None else la.gemm(xh_pick, w_final, tb=True, exact=True)
+            mse_ar = la.mse(la.gemm(xr, q_used, tb=True, exact=True), ref2)
+            mse_ag = la.mse(la.gemm(xg, q_used, tb=True, exact=True), ref2)
             if mse_ag < mse_ar:
                 u_act = Ua
                 gptq_act = 1
             else:
                 order = None
 
+    ph.mark("act_gptq")
     # ---- weight lattice refinement and Gram carries (solution.py:986-1015)
     e4h = int(la.abs_sum_f64(w) * 1e3) % 2 == 0
     e4 = C <= 4096
@@ -233,9 +261,12 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         except L.Hif4xError:
             gw = gwf = None
 
+    ph.mark("refine_grams")
     if info is not None:
+        info["phases_ms"] = ph.result()
         info.update(alpha=best_alpha, mode=mode, gptq_w=gptq_w, gptq_act=gptq_act, e3=refined, tmax=tmax,
                     w_final=w_final, q_used=q_used, s=s)
+    la.check_device_status(dev)
     activation_state = {
         "s": s.cpu().contiguous(),
         "mode": mode,
@@ -252,8 +283,8 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
 def refine_act_values(x, values, unit, gw, gwf) -> torch.Tensor:
     """_refine_act_values (solution.py:621-663)."""
     v4, d = la.refine_prep(values, unit)
-    M = la.gemm(la.mul(v4, d), gw)
-    la.gemm(x, gwf, alpha=-1.0, beta=1.0, out=M)
+    M = la.gemm(la.mul(v4, d), gw, exact=True)
+    la.gemm(x, gwf, alpha=-1.0, beta=1.0, out=M, exact=True)
     T = values.shape[0]
     n_sweeps = 40 if T <= 256 else 18 if T <= 512 else 7
     rounds = n_sweeps * REFINE_ACT_ROUNDS
@@ -306,4 +337,5 @@ def dynamic_activation(activation_quant: torch.Tensor, activation_scale: torch.T
                 result = None
     if result is None:
         result = codec.values_to_params(values, p) if values is not None else p
+    la.check_device_status(dev)
     return result if return_device else result.reference()

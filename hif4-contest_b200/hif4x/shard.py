@@ -1,0 +1,103 @@
+"""Sharding the weight-set conversion across the GPUs of one node.
+
+Whole matrices are independent (each has its own Hessians, Hinv and
+states), so a weight set is split by longest-processing-time-first (LPT)
+over the ranks, by the cost model  N*C^2 + 3*C^3 + T*C^2  (GPTQ trailing
+updates, three Cholesky/inverse factorisations, Grams), and each rank
+converts its own matrices with no collective on the data path.  The only
+collective is the gather of the converted, packed HiF4 shards (4.5 bit per
+element) to one rank at the end, over NCCL.
+"""
+from __future__ import annotations
+
+import heapq
+from dataclasses import dataclass
+
+import torch
+
+# Llama-3-8B decoder layer: name -> (out_features N, in_features C, input id)
+LLAMA3_8B_LAYER = {
+    "q_proj": (4096, 4096, "attn_in"), "k_proj": (1024, 4096, "attn_in"), "v_proj": (1024, 4096, "attn_in"),
+    "o_proj": (4096, 4096, "attn_out"), "gate_proj": (14336, 4096, "mlp_in"), "up_proj": (14336, 4096, "mlp_in"),
+    "down_proj": (4096, 14336, "mlp_act"),
+}
+
+
+@dataclass(frozen=True)
+class MatrixJob:
+    layer: int
+    name: str
+    N: int
+    C: int
+    input_id: str
+
+    @property
+    def key(self) -> str:
+        return f"layers.{self.layer}.{self.name}"
+
+
+def matrix_cost(N: int, C: int, T_cal: int) -> float:
+    return float(N) * C * C + 3.0 * C ** 3 + float(T_cal) * C * C
+
+
+def model_jobs(layers: int, shapes: dict = LLAMA3_8B_LAYER) -> list[MatrixJob]:
+    return [MatrixJob(l, n, N, C, i) for l in range(layers) for n, (N, C, i) in shapes.items()]
+
+
+def lpt_assign(costs: list[float], world: int) -> list[int]:
+    """Rank of each item: biggest first onto the least-loaded rank (ties: lower rank)."""
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    heap = [(0.0, r) for r in range(world)]
+    heapq.heapify(heap)
+    owner = [0] * len(costs)
+    for i in order:
+        load, r = heapq.heappop(heap)
+        owner[i] = r
+        heapq.heappush(heap, (load + costs[i], r))
+    return owner
+
+
+def rank_jobs(jobs: list[MatrixJob], rank: int, world: int, T_cal: int) -> list[MatrixJob]:
+    owner = lpt_assign([matrix_cost(j.N, j.C, T_cal) for j in jobs], world)
+    return [j for j, o in zip(jobs, owner) if o == rank]
+
+
+def pack_params(p: dict) -> torch.Tensor:
+    """dict5 (CPU, reference shapes) -> one uint8 buffer: packed HiF4 (meta + codes)."""
+    from . import codec
+    sf = p["scale_factor"]
+    R, nb = sf.shape[0], sf.shape[1]
+    C = nb * 64
+    dev = torch.device("cuda", torch.cuda.current_device())
+    d5 = codec.Dict5(sf.reshape(R, nb).to(dev).contiguous(), p["scale_lv2"].reshape(R, nb, 8).to(dev).contiguous(),
+                     p["scale_lv3"].reshape(R, nb, 16).to(dev).contiguous(),
+                     p["sign"].reshape(R, C).to(dev).contiguous(), p["mant"].reshape(R, C).to(dev).contiguous())
+    meta, codes = codec.pack(d5)
+    return torch.cat([meta.view(torch.uint8).reshape(-1), codes.reshape(-1)])
+
+
+def gather_shards(local: dict[str, torch.Tensor], dist, device) -> dict[str, torch.Tensor] | None:
+    """All ranks: contribute {key: uint8 CUDA buffer}; rank 0 receives every
+    rank's buffers (one all_gather of sizes, one of padded payloads, NCCL)."""
+    world = dist.get_world_size()
+    keys = sorted(local)
+    payload = torch.cat([local[k] for k in keys]) if keys else torch.zeros(0, dtype=torch.uint8, device=device)
+    n = torch.tensor([payload.numel()], dtype=torch.int64, device=device)
+    sizes = [torch.zeros(1, dtype=torch.int64, device=device) for _ in range(world)]
+    dist.all_gather(sizes, n)
+    mx = int(max(int(s.item()) for s in sizes))
+    buf = torch.zeros(mx, dtype=torch.uint8, device=device)
+    buf[:payload.numel()] = payload
+    outs = [torch.empty(mx, dtype=torch.uint8, device=device) for _ in range(world)]
+    dist.all_gather(outs, buf)
+    meta = [None] * world
+    dist.all_gather_object(meta, [(k, int(local[k].numel())) for k in keys])
+    if dist.get_rank() != 0:
+        return None
+    res = {}
+    for r in range(world):
+        off = 0
+        for k, sz in meta[r]:
+            res[k] = outs[r][off:off + sz]
+            off += sz
+    return res

@@ -168,6 +168,26 @@ int hif4x_gemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, con
                int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C, int64_t ldc,
                int64_t strideC, int64_t batch, void *stream);
 
+/* The same GEMM on the CUDA cores only: round-to-nearest fp32 FMAs, for
+ * products whose result is differenced against another product (the guard
+ * MSEs and the refinement residual image, solution.py:637, 868, 906, 930-931,
+ * 970-971), where the tensor cores' truncating accumulation would be
+ * amplified by cancellation. */
+int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                    int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
+                    int64_t ldc, int64_t strideC, int64_t batch, void *stream);
+
+/* Tensor-core form of hif4x_gemm (batch 1): tcgen05.mma kind::tf32 with
+ * operands split hi + lo (3 products, fp32-faithful), TMA-fed, accumulators
+ * in tensor memory.  Needs 16-byte aligned A/B and lda, ldb % 4 == 0, else
+ * returns HIF4X_ERR_UNSUPPORTED.  hif4x_gemm uses it for large products. */
+int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                  const float *B, int64_t ldb, float beta, float *C, int64_t ldc, void *stream);
+
+/* Synchronises the stream; returns (and clears) the sticky device status:
+ * HIF4X_TIMEOUT if a bounded device-side wait expired since the last call. */
+int hif4x_device_status(void *stream);
+
 /* _upper_cholesky_inv (example/solution/solution.py:287-300): U upper with
  * U^T U = (H + damp * max(mean(diag H), 1e-30) I)^-1, for `batch` n x n
  * matrices.  Computed as one Cholesky of the index-reversed matrix and one

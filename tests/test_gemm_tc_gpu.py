@@ -1,0 +1,47 @@
+"""The tcgen05 (3xTF32) GEMM against an fp64 torch reference: every operand
+major (ta, tb), ragged M/N/K tails, alpha/beta, and no device-status
+timeout afterwards.  Tolerance is the fp32-GEMM bound the SIMT tests use,
+2e-6 * sqrt(K) * max|C|: the tensor core accumulates in fp32 with truncation,
+so its error grows with K like a long fp32 dot product."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from hif4x import _lib as L  # noqa: E402
+
+
+def rnd(*shape, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g).cuda()
+
+
+def tc_gemm(A, B, ta, tb, alpha=1.0, beta=0.0, C=None):
+    M = A.shape[1] if ta else A.shape[0]
+    K = A.shape[0] if ta else A.shape[1]
+    N = B.shape[0] if tb else B.shape[1]
+    if C is None:
+        C = torch.zeros(M, N, device="cuda")
+    st = L.call("hif4x_gemm_tc", int(ta), int(tb), M, N, K, L.f32(alpha), L.ptr(A), A.stride(0), L.ptr(B),
+                B.stride(0), L.f32(beta), L.ptr(C), C.stride(0), L.stream())
+    assert st == L.OK
+    return C
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 1), (0, 0), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (256, 384, 512), (300, 200, 1000), (1024, 1024, 4096)])
+def test_tc_gemm_vs_fp64(ta, tb, M, N, K):
+    A = rnd(K, M, seed=1) if ta else rnd(M, K, seed=1)
+    B = rnd(N, K, seed=2) if tb else rnd(K, N, seed=2)
+    ref = (A.double().T if ta else A.double()) @ (B.double().T if tb else B.double())
+    got = tc_gemm(A, B, ta, tb)
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    err = float((got.double() - ref).abs().max() / ref.abs().max())
+    assert err < 2e-6 * K ** 0.5 + 1e-6, err
+
+
+def test_tc_gemm_alpha_beta():
+    A, B, C = rnd(256, 512, seed=3), rnd(512, 256, seed=4), rnd(256, 256, seed=5)
+    ref = -1.0 * (A.double() @ B.double()) + 1.0 * C.double()
+    got = tc_gemm(A, B, 0, 0, alpha=-1.0, beta=1.0, C=C.clone())
+    assert float((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * 512 ** 0.5 + 1e-6
