@@ -117,6 +117,7 @@ struct TcArgs {
   float *C;
   int64_t ldc;
   int a_mn, b_mn;   // operand majors: 1 = M/N contiguous in global (and smem)
+  int lower;        // 1: only tiles touching the lower triangle (n0 <= m0 + BM - 1)
 };
 
 // operand tile loads for one stage (K-major: one 128x32 box; MN-major: four 32x32 boxes)
@@ -154,6 +155,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int nk = (int)((args.K + BK - 1) / BK);
+  if (args.lower && n0 > m0 + BM - 1) return;   // tile strictly above the diagonal: nothing to do
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -332,9 +334,18 @@ using namespace hif4x;
 // when the operands do not meet the TMA rules (16-byte aligned bases,
 // leading dimensions a multiple of 4 floats), so the caller can take the
 // SIMT kernel instead.
+int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream);
+
 extern "C" int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
                              int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
                              void *stream) {
+  return hif4x_gemm_tc_ex(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, 0, stream);
+}
+
+// Same, optionally restricted to output tiles that touch the lower triangle.
+int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return HIF4X_ERR_ARG;
   auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!al16(A) || !al16(B) || (lda & 3) || (ldb & 3)) return HIF4X_ERR_UNSUPPORTED;
@@ -346,7 +357,7 @@ extern "C" int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, fl
   // B: tb = 1 -> stored N x K (K-major); tb = 0 -> stored K x N (MN-major)
   const bool okB = tb ? tc::make_map(&mb, B, K, N, ldb, 32, 128, KSW) : tc::make_map(&mb, B, N, K, ldb, 32, 32, MNSW);
   if (!okA || !okB) return HIF4X_ERR_UNSUPPORTED;
-  tc::TcArgs args{M, N, K, alpha, beta, C, ldc, ta ? 1 : 0, tb ? 0 : 1};
+  tc::TcArgs args{M, N, K, alpha, beta, C, ldc, ta ? 1 : 0, tb ? 0 : 1, lower ? 1 : 0};
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(tc::gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);

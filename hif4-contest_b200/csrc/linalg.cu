@@ -28,6 +28,7 @@ struct GemmArgs {
   int64_t ldb, sB;
   float *C;
   int64_t ldc, sC;
+  int lower;   // 1: skip output tiles strictly above the diagonal
 };
 
 __global__ void __launch_bounds__(GTHREADS) gemm_kernel(const GemmArgs g) {
@@ -38,6 +39,7 @@ __global__ void __launch_bounds__(GTHREADS) gemm_kernel(const GemmArgs g) {
   const float *B = g.B + bz * g.sB;
   float *C = g.C + bz * g.sC;
   const int64_t m0 = (int64_t)blockIdx.y * GBM, n0 = (int64_t)blockIdx.x * GBN;
+  if (g.lower && n0 > m0 + GBM - 1) return;
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;  // 16 x 16 threads, each 8x8 outputs
 
@@ -206,26 +208,86 @@ __global__ void __launch_bounds__(128) trsm_panel_kernel(float *A, int64_t ld, i
     if (j < b) row[j] = x[j];
 }
 
-// In-place inverse of a small lower-triangular block (b <= CB); one CTA.
-__global__ void __launch_bounds__(CB) trtri_diag_kernel(float *A, int64_t ld, int64_t k, int b) {
-  __shared__ float L[CB][CB + 1];
-  __shared__ float X[CB][CB + 1];
-  for (int e = threadIdx.x; e < b * b; e += blockDim.x) L[e / b][e % b] = A[(k + e / b) * ld + k + e % b];
+// Factor (optional) and invert one lower-triangular block of b <= 128 rows in
+// shared memory, one CTA of 1024 threads.
+//   do_factor: A's b x b block (leading dim ld) is SPD: Cholesky in place
+//   (right-looking, one column per step), L written back with zeros above the
+//   diagonal; info = 1 on a non-positive pivot.  Otherwise A already holds L.
+//   Then X = L^-1 by forward substitution, 8 lanes per column (warp shuffles,
+//   columns are independent so only warp-level syncs are needed), written to
+//   Linv (leading dim ldi; may alias A).
+constexpr int PB = 128;
+__global__ void __launch_bounds__(1024) potrf_inv128_kernel(float *A, int64_t ld, int b, float *Linv, int64_t ldi,
+                                                            int *info, int mode) {
+  const int do_factor = mode & 1, do_invert = mode & 2;
+  extern __shared__ float sm[];
+  float *S = sm;                   // [PB][PB + 1]
+  float *X = sm + PB * (PB + 1);   // [PB][PB + 1]
+  const int tid = threadIdx.x;
+  for (int e = tid; e < b * b; e += blockDim.x) {
+    const int r = e / b, c = e % b;
+    S[r * (PB + 1) + c] = (c <= r) ? A[r * ld + c] : 0.0f;
+  }
   __syncthreads();
-  // column c of X solves L x = e_c (forward substitution), one thread per column
-  const int c = threadIdx.x;
-  if (c < b) {
-    for (int i = 0; i < b; i++) {
-      float s = (i == c) ? 1.0f : 0.0f;
-      for (int j = c; j < i; j++) s = fmaf(-L[i][j], X[j][c], s);
-      X[i][c] = (i < c) ? 0.0f : s / L[i][i];
+  if (do_factor) {
+    for (int j = 0; j < b; j++) {
+      if (tid == 0) {
+        const float p = S[j * (PB + 1) + j];
+        if (!(p > 0.0f) || !isfinite(p)) {
+          atomicExch(info, 1);
+          S[j * (PB + 1) + j] = 1.0f;
+        } else {
+          S[j * (PB + 1) + j] = sqrtf(p);
+        }
+      }
+      __syncthreads();
+      const float djj = S[j * (PB + 1) + j];
+      for (int i = j + 1 + tid; i < b; i += blockDim.x) S[i * (PB + 1) + j] = S[i * (PB + 1) + j] / djj;
+      __syncthreads();
+      // rank-1 update of the trailing lower triangle: thread (ty, tx) of a
+      // 32 x 32 grid walks rows j+1+ty and columns j+1+tx in steps of 32
+      const int tx = tid & 31, ty = tid >> 5;
+      for (int r = j + 1 + ty; r < b; r += 32) {
+        const float srj = S[r * (PB + 1) + j];
+        for (int c = j + 1 + tx; c <= r; c += 32)
+          S[r * (PB + 1) + c] = fmaf(-srj, S[c * (PB + 1) + j], S[r * (PB + 1) + c]);
+      }
+      __syncthreads();
+    }
+    for (int e = tid; e < b * b; e += blockDim.x) {
+      const int r = e / b, c = e % b;
+      A[r * ld + c] = (c <= r) ? S[r * (PB + 1) + c] : 0.0f;
     }
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-    const int r = e / b, cc = e % b;
-    A[(k + r) * ld + k + cc] = (cc <= r) ? X[r][cc] : 0.0f;
+  if (!do_invert) return;
+  // inverse: column c = tid / 8, sub-lane sl = tid % 8
+  const int c = tid >> 3, sl = tid & 7;
+  for (int i = 0; i < b; i++) {
+    float part = 0.0f;
+    if (c < b && i > c)
+      for (int j = c + sl; j < i; j += 8) part = fmaf(S[i * (PB + 1) + j], X[j * (PB + 1) + c], part);
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    part += __shfl_xor_sync(0xffffffffu, part, 4);
+    if (sl == 0 && c < b) X[i * (PB + 1) + c] = (i < c) ? 0.0f : ((i == c ? 1.0f : 0.0f) - part) / S[i * (PB + 1) + i];
+    __syncwarp();
   }
+  __syncthreads();
+  for (int e = tid; e < b * b; e += blockDim.x) {
+    const int r = e / b, cc = e % b;
+    Linv[r * ldi + cc] = (cc <= r) ? X[r * (PB + 1) + cc] : 0.0f;
+  }
+}
+
+// mode bits: 1 = factor A in place, 2 = write L^-1 to Linv
+static int potrf_inv128(float *A, int64_t ld, int b, float *Linv, int64_t ldi, int *info, int mode,
+                        cudaStream_t s) {
+  const int smem = (int)(2 * PB * (PB + 1) * sizeof(float));
+  if (cudaFuncSetAttribute(potrf_inv128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return HIF4X_ERR_LAUNCH;
+  potrf_inv128_kernel<<<1, 1024, smem, s>>>(A, ld, b, Linv, ldi, info, mode);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
 }
 
 // out[i][j] = in[n-1-i][n-1-j] (batched, square)
@@ -271,6 +333,69 @@ __global__ void zero_upper_kernel(float *A, int64_t n, int64_t total) {
 // for j > i inside the block (example/solution/solution.py:316-326).
 constexpr int GQ_THREADS = 128;
 constexpr int GQ_BLK = 128;
+constexpr int GQW_WARPS = 8;   // rows per CTA in the warp-per-row kernel
+
+// Warp-per-row form: lane l owns block columns l, l+32, l+64, l+96 in
+// registers; column i's owner quantizes it and broadcasts the scaled error,
+// every lane updates its own later columns.  U's block sits in shared memory.
+__global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_warp_kernel(float *W, const float *unit, const float *U,
+                                                                         float *Q, float *E, int64_t R, int64_t C,
+                                                                         int64_t i1, int nb, int64_t bstride_rows,
+                                                                         int64_t bstride_u) {
+  extern __shared__ float Hs[];   // [nb][nb]
+  const int64_t bz = blockIdx.y;
+  W += bz * bstride_rows * C;
+  unit += bz * bstride_rows * C;
+  Q += bz * bstride_rows * C;
+  E += bz * bstride_rows * GQ_BLK;
+  U += bz * bstride_u;
+  for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * GQW_WARPS + (threadIdx.x >> 5);
+  if (r >= R) return;
+  float w[4], u[4], q[4], err[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int c = lane + 32 * k;
+    w[k] = c < nb ? W[r * C + i1 + c] : 0.0f;
+    u[k] = c < nb ? unit[r * C + i1 + c] : 1.0f;
+    q[k] = 0.0f;
+    err[k] = 0.0f;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    for (int ii = 0; ii < 32; ii++) {
+      const int i = 32 * k + ii;
+      if (i >= nb) break;
+      float ei = 0.0f;
+      if (lane == ii) {
+        const float wi = w[k], ui = u[k];
+        float m = rintf(__fmul_rn(__fdiv_rn(fabsf(wi), ui), 4.0f));
+        m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
+        const float qi = __fmul_rn(__fmul_rn(wi >= 0.0f ? 1.0f : -1.0f, m), ui);
+        q[k] = qi;
+        ei = __fdiv_rn(__fsub_rn(wi, qi), fmaxf(Hs[i * nb + i], 1e-30f));
+        err[k] = ei;
+      }
+      ei = __shfl_sync(0xffffffffu, ei, ii);
+      const float *hrow = Hs + i * nb;
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const int c = lane + 32 * kk;
+        if (kk >= k && c > i && c < nb) w[kk] = fmaf(-ei, hrow[c], w[kk]);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int c = lane + 32 * k;
+    if (c < nb) {
+      Q[r * C + i1 + c] = q[k];
+      E[r * GQ_BLK + c] = err[k];
+    }
+  }
+}
 
 __global__ void __launch_bounds__(GQ_THREADS) gptq_block_kernel(float *W, const float *unit, const float *U,
                                                                   float *Q, float *E, int64_t R, int64_t C,
@@ -425,9 +550,18 @@ extern "C" int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, fl
 extern "C" int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
                                int64_t lda, int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta,
                                float *C, int64_t ldc, int64_t strideC, int64_t batch, void *stream);
+int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream);
+static int gemm_simt_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                        int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
+                        int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream);
 
 // Products of at least this many multiply-adds go to the tensor cores.
 static const int64_t kTcMinMacs = int64_t(1) << 26;
+
+static int gemm_dispatch(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                         int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
+                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream);
 
 static bool tc_disabled() {
   static const bool off = [] {
@@ -443,21 +577,35 @@ extern "C" int hif4x_gemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float
   if (M < 0 || N < 0 || K < 0 || batch < 0) return HIF4X_ERR_ARG;
   if (M == 0 || N == 0 || batch == 0) return HIF4X_OK;
   if (!A || !B || !C || batch > 65535) return HIF4X_ERR_ARG;
+  return gemm_dispatch(ta, tb, M, N, K, alpha, A, lda, strideA, B, ldb, strideB, beta, C, ldc, strideC, batch, 0,
+                       stream);
+}
+
+static int gemm_dispatch(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                         int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
+                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream) {
   if (batch == 1 && K >= 64 && M * N * K >= kTcMinMacs && !tc_disabled()) {
-    const int st = hif4x_gemm_tc(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, stream);
+    const int st = hif4x_gemm_tc_ex(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, lower, stream);
     if (st != HIF4X_ERR_UNSUPPORTED) return st;
   }
-  return hif4x_gemm_simt(ta, tb, M, N, K, alpha, A, lda, strideA, B, ldb, strideB, beta, C, ldc, strideC, batch,
-                         stream);
+  return gemm_simt_ex(ta, tb, M, N, K, alpha, A, lda, strideA, B, ldb, strideB, beta, C, ldc, strideC, batch, lower,
+                      stream);
 }
 
 extern "C" int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
                                int64_t lda, int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta,
                                float *C, int64_t ldc, int64_t strideC, int64_t batch, void *stream) {
+  return gemm_simt_ex(ta, tb, M, N, K, alpha, A, lda, strideA, B, ldb, strideB, beta, C, ldc, strideC, batch, 0,
+                      stream);
+}
+
+static int gemm_simt_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
+                        int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
+                        int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream) {
   if (M < 0 || N < 0 || K < 0 || batch < 0) return HIF4X_ERR_ARG;
   if (M == 0 || N == 0 || batch == 0) return HIF4X_OK;
   if (!A || !B || !C || batch > 65535) return HIF4X_ERR_ARG;
-  GemmArgs g{ta, tb, M, N, K, alpha, beta, A, lda, strideA, B, ldb, strideB, C, ldc, strideC};
+  GemmArgs g{ta, tb, M, N, K, alpha, beta, A, lda, strideA, B, ldb, strideB, C, ldc, strideC, lower};
   dim3 grid(nblk(N, GBN), nblk(M, GBM), (unsigned)batch);
   if (grid.y > 65535) return HIF4X_ERR_ARG;
   gemm_kernel<<<grid, GTHREADS, 0, (cudaStream_t)stream>>>(g);
@@ -465,17 +613,18 @@ extern "C" int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, 
   return HIF4X_OK;
 }
 
-// Lower Cholesky in place (row-major, ld = n), blocked right-looking.
-static int potrf_lower(float *A, int64_t n, int *info_dev, cudaStream_t s) {
+// Lower Cholesky in place of the n x n block at A (row-major, leading dim
+// ld), blocked right-looking with 64-wide panels.
+static int potrf_lower_ld(float *A, int64_t n, int64_t ld, int *info_dev, cudaStream_t s) {
   for (int64_t k = 0; k < n; k += CB) {
     const int b = (int)std::min<int64_t>(CB, n - k);
-    potrf_diag_kernel<<<1, 256, 0, s>>>(A, n, k, b, info_dev);
+    potrf_diag_kernel<<<1, 256, 0, s>>>(A, ld, k, b, info_dev);
     const int64_t rest = n - k - b;
     if (rest > 0) {
-      trsm_panel_kernel<<<nblk(rest, 128), 128, 0, s>>>(A, n, n, k, b);
+      trsm_panel_kernel<<<nblk(rest, 128), 128, 0, s>>>(A, ld, n, k, b);
       // trailing update A22 -= P P^T  (P = A[k+b:, k:k+b])
-      const float *P = A + (k + b) * n + k;
-      int st = hif4x_gemm(0, 1, rest, rest, b, -1.0f, P, n, 0, P, n, 0, 1.0f, A + (k + b) * n + (k + b), n, 0, 1, s);
+      const float *P = A + (k + b) * ld + k;
+      int st = hif4x_gemm(0, 1, rest, rest, b, -1.0f, P, ld, 0, P, ld, 0, 1.0f, A + (k + b) * ld + (k + b), ld, 0, 1, s);
       if (st) return st;
     }
   }
@@ -483,15 +632,54 @@ static int potrf_lower(float *A, int64_t n, int *info_dev, cudaStream_t s) {
   return HIF4X_OK;
 }
 
+static int potrf_lower(float *A, int64_t n, int *info_dev, cudaStream_t s) {
+  return potrf_lower_ld(A, n, n, info_dev, s);
+}
+
+// dst (rows x cols, ldd) = src (lds); zero_upper clears dst[i][j] for j > i.
+__global__ void copy2d_kernel(const float *src, int64_t lds, float *dst, int64_t ldd, int64_t rows, int64_t cols,
+                              int zero_upper) {
+  const int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (e >= rows * cols) return;
+  const int64_t r = e / cols, c = e % cols;
+  dst[r * ldd + c] = (zero_upper && c > r) ? 0.0f : src[r * lds + c];
+}
+
+static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_t s);
+
+// Recursive lower Cholesky in place of the n x n block at A (leading dim ld):
+//   L11 = chol(A11);  L21 = A21 L11^-T;  L22 = chol(A22 - L21 L21^T).
+// L21 is one GEMM against L11's inverse and the update one large-K GEMM over
+// the lower-triangle tiles, so almost all flops run as big tensor-core GEMMs;
+// leaves of <= 128 rows are factored in shared memory by one CTA.  The upper
+// triangle is left stale (cleared by the caller).
+// Split n1 = n/2 rounded down to a multiple of 128 (at least 128), so
+// n1 <= n/2 and the workspace n1*n1 + max(n2*n1, n1*n1/4) is at most n*n/2
+// floats (the recursive calls reuse it after this level is done with it).
+static int potrf_rec(float *A, int64_t n, int64_t ld, int *info_dev, float *work, cudaStream_t s) {
+  if (n <= PB) return potrf_inv128(A, ld, (int)n, nullptr, 0, info_dev, 1, s);
+  const int64_t n1 = std::max<int64_t>(PB, (n / 2 / PB) * PB), n2 = n - n1;
+  float *A11 = A, *A21 = A + n1 * ld, *A22 = A + n1 * ld + n1;
+  int st = potrf_rec(A11, n1, ld, info_dev, work, s);
+  if (st) return st;
+  float *Linv = work;             // n1 x n1
+  float *T = work + n1 * n1;      // n2 x n1, and trtri's n1*n1/4 scratch before that
+  copy2d_kernel<<<nblk(n1 * n1, 256), 256, 0, s>>>(A11, ld, Linv, n1, n1, n1, 1);
+  st = trtri_lower(Linv, n1, n1, T, s);
+  if (st) return st;
+  st = gemm_dispatch(0, 1, n2, n1, n1, 1.0f, A21, ld, 0, Linv, n1, 0, 0.0f, T, n1, 0, 1, 0, s);   // T = A21 L11^-T
+  if (st) return st;
+  copy2d_kernel<<<nblk(n2 * n1, 256), 256, 0, s>>>(T, n1, A21, ld, n2, n1, 0);
+  st = gemm_dispatch(0, 1, n2, n2, n1, -1.0f, A21, ld, 0, A21, ld, 0, 1.0f, A22, ld, 0, 1, 1, s);
+  if (st) return st;
+  return potrf_rec(A22, n2, ld, info_dev, work, s);
+}
+
 // In-place inverse of a lower-triangular n x n block at A (leading dim ld):
 // inv([[A11, 0], [A21, A22]]) = [[A11^-1, 0], [-A22^-1 A21 A11^-1, A22^-1]].
 static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_t s) {
-  if (n <= CB) {
-    trtri_diag_kernel<<<1, CB, 0, s>>>(A, ld, 0, (int)n);
-    HIF4X_CHECK_LAUNCH();
-    return HIF4X_OK;
-  }
-  int64_t n1 = ((n / 2 + CB - 1) / CB) * CB;
+  if (n <= PB) return potrf_inv128(A, ld, (int)n, A, ld, nullptr, 2, s);
+  int64_t n1 = ((n / 2 + PB - 1) / PB) * PB;
   const int64_t n2 = n - n1;
   float *A11 = A, *A21 = A + n1 * ld, *A22 = A + n1 * ld + n1;
   int st = trtri_lower(A11, n1, ld, work, s);
@@ -516,11 +704,17 @@ extern "C" int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, fl
     float *scratch = work + nn;
     reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(H + b * nn, P, n, nn);
     damp_diag_kernel<<<1, 1024, 0, s>>>(P, n, damp);
-    int st = potrf_lower(P, n, info_dev, s);
-    if (st) return st;
-    zero_upper_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, n, nn);
-    st = trtri_lower(P, n, n, scratch, s);
-    if (st) return st;
+    int st;
+    if (n <= PB) {
+      st = potrf_inv128(P, n, (int)n, P, n, info_dev, 3, s);   // L^-1 in place
+      if (st) return st;
+    } else {
+      st = potrf_rec(P, n, n, info_dev, scratch, s);
+      if (st) return st;
+      zero_upper_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, n, nn);
+      st = trtri_lower(P, n, n, scratch, s);
+      if (st) return st;
+    }
     reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, U + b * nn, n, nn);
   }
   HIF4X_CHECK_LAUNCH();
@@ -542,13 +736,14 @@ extern "C" int hif4x_gptq(const float *X, const float *unit, const float *U, int
   float *E = work + batch * R * C;
   if (cudaMemcpyAsync(W, X, sizeof(float) * batch * R * C, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return HIF4X_ERR_LAUNCH;
-  const size_t smem = sizeof(float) * (GQ_BLK * GQ_BLK + GQ_BLK * GQ_THREADS);
-  if (cudaFuncSetAttribute(gptq_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  const size_t smem = sizeof(float) * GQ_BLK * GQ_BLK;
+  if (cudaFuncSetAttribute(gptq_block_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
     return HIF4X_ERR_LAUNCH;
   for (int64_t i1 = 0; i1 < C; i1 += GQ_BLK) {
     const int nb = (int)std::min<int64_t>(GQ_BLK, C - i1);
-    dim3 grid(nblk(R, GQ_THREADS), (unsigned)batch);
-    gptq_block_kernel<<<grid, GQ_THREADS, smem, s>>>(W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
+    dim3 grid(nblk(R, GQW_WARPS), (unsigned)batch);
+    gptq_block_warp_kernel<<<grid, GQW_WARPS * 32, smem, s>>>(W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
     HIF4X_CHECK_LAUNCH();
     const int64_t i2 = i1 + nb;
     if (i2 < C) {

@@ -39,7 +39,7 @@ def test_gemm_accumulate_strided_batched():
     assert torch.allclose(got.double(), ref, atol=1e-4, rtol=1e-5)
 
 
-@pytest.mark.parametrize("n", [64, 100, 256, 1000])
+@pytest.mark.parametrize("n", [64, 100, 256, 1000, 1536, 2176])
 def test_chol_upper_inv(n):
     X = rnd(3 * n, n, seed=n)
     H = X.T @ X
