@@ -134,20 +134,36 @@ __device__ __forceinline__ void load_group(const ConvParams &p, int64_t g, float
 // out[e] = sum_{d=0..63} x[d] * (H64[d][e] / 8 * sign_e), summed d = 0..63
 // from +0 as torch's CPU einsum does (solution.py:243-245).
 // `stage` is the thread's transposed shared-memory column (stride `st`).
-__device__ __forceinline__ void rot64_exact(float (&x)[64], uint64_t sgn, float *stage, int st) {
+__device__ __forceinline__ void rot64_exact(float (&x)[64], uint64_t sgn, float *stage, int st, bool bf16_vals) {
   // Exactness test: all x are multiples of 2^L; if sum|x| < 2^(L+23) every
   // partial sum of any order is representable, so the FWHT equals the
   // sequential sum bit for bit.
   int L = 1 << 20;
   float S = 0.0f;
+  if (bf16_vals) {
+    // bf16-valued inputs (NVFP4 decode): a normal value's lowest set bit is at
+    // least its exponent - 7, so L = exponent(min nonzero |x|) - 7 bounds it
+    float mn = INFINITY;
 #pragma unroll
-  for (int k = 0; k < 64; k++) {
-    const uint32_t b = __float_as_uint(x[k]);
-    const int ef = (int)((b >> 23) & 255u);
-    const uint32_t m = (b & 0x7fffffu) | 0x800000u;
-    const int lsb = (b & 0x7fffffffu) == 0u ? (1 << 20) : (ef == 0 ? -(1 << 20) : ef - 150 + (__ffs((int)m) - 1));
-    L = min(L, lsb);
-    S = __fadd_rn(S, fabsf(x[k]));
+    for (int k = 0; k < 64; k++) {
+      const float a = fabsf(x[k]);
+      mn = fminf(mn, a == 0.0f ? INFINITY : a);
+      S = __fadd_rn(S, a);
+    }
+    if (mn != INFINITY) {
+      const int ef = (int)(__float_as_uint(mn) >> 23);
+      L = ef == 0 ? -(1 << 20) : ef - 134;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 64; k++) {
+      const uint32_t b = __float_as_uint(x[k]);
+      const int ef = (int)((b >> 23) & 255u);
+      const uint32_t m = (b & 0x7fffffu) | 0x800000u;
+      const int lsb = (b & 0x7fffffffu) == 0u ? (1 << 20) : (ef == 0 ? -(1 << 20) : ef - 150 + (__ffs((int)m) - 1));
+      L = min(L, lsb);
+      S = __fadd_rn(S, fabsf(x[k]));
+    }
   }
   const bool fast = (L >= -120) && (L + 23 > 127 || S < exp2i(L + 23));
   if (fast) {
@@ -202,11 +218,55 @@ struct Enc {
 // range, so the 6 candidates x 3 lv units collapse onto 14 distinct units
 // sig * 2^(e0+m) (sig in {1, 1.25, 1.5, 1.75}; m in 0..3 for sig 1, 1.25
 // and 0..2 for 1.5, 1.75), each evaluated once per element.
-__device__ __forceinline__ Enc search_fast(const float *stage, int st, int e0) {
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic, round-to-nearest per lane)
+typedef unsigned long long u64;
+__device__ __forceinline__ u64 pk2(float lo, float hi) {
+  u64 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(u64 v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
+  u64 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b) {
+  u64 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+  u64 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// The per-element unit work runs on f32x2 pairs; each lane is an IEEE RN fp32
+// operation, so values and order equal the scalar restatement.  Pairs
+// (sig s, scale m):
+//   A:(1,m)+(2,m) m=0,1,2 share the packed Markstein quotient {q(1.25), q(1.5)}
+//   B:(0,0)+(0,1)  C:(0,2)+(0,3)  D:(3,0)+(3,1)  E:(3,2)+(1,3)
+// The squared error is computed as fma(m4, -u/4, |x|)^2 (the negated
+// difference, same square).
+__device__ __forceinline__ Enc search_fast2(const float *stage, int st, int e0) {
   const float p2 = exp2i(e0);
   const float u[4] = {p2, __fmul_rn(p2, 1.25f), __fmul_rn(p2, 1.5f), __fmul_rn(p2, 1.75f)};
   const float y[4] = {exp2i(-e0), __fdiv_rn(1.0f, u[1]), __fdiv_rn(1.0f, u[2]), __fdiv_rn(1.0f, u[3])};
-  // quarter units uq[s][m] = u[s] * 2^(m-2)
+  auto qsc = [](int m) { return m == 0 ? 4.0f : m == 1 ? 2.0f : m == 2 ? 1.0f : 0.5f; };
+  auto nuq = [&](int s, int m) { return -__fmul_rn(u[s], m == 0 ? 0.25f : m == 1 ? 0.5f : m == 2 ? 1.0f : 2.0f); };
+  const u64 Y12 = pk2(y[1], y[2]), NU12 = pk2(-u[1], -u[2]);
+  const u64 MAG2 = pk2(kMagic, kMagic), NMAG2 = pk2(-kMagic, -kMagic);
+  // per pair: scale {qs_lo, qs_hi} and negated quarter unit {-uq_lo, -uq_hi}
+  const u64 QS_A[3] = {pk2(qsc(0), qsc(0)), pk2(qsc(1), qsc(1)), pk2(qsc(2), qsc(2))};
+  const u64 NU_A[3] = {pk2(nuq(1, 0), nuq(2, 0)), pk2(nuq(1, 1), nuq(2, 1)), pk2(nuq(1, 2), nuq(2, 2))};
+  const u64 QS_B = pk2(qsc(0), qsc(1)), NU_B = pk2(nuq(0, 0), nuq(0, 1));
+  const u64 QS_C = pk2(qsc(2), qsc(3)), NU_C = pk2(nuq(0, 2), nuq(0, 3));
+  const u64 QS_D = pk2(qsc(0), qsc(1)), NU_D = pk2(nuq(3, 0), nuq(3, 1));
+  const u64 QS_E = pk2(qsc(2), qsc(3)), NU_E = pk2(nuq(3, 2), nuq(1, 3));
+  const float M7 = kMagic + 7.0f;
   float err[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   uint32_t bits[6] = {0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll 1
@@ -214,31 +274,40 @@ __device__ __forceinline__ Enc search_fast(const float *stage, int st, int e0) {
     float Q[2][14];
 #pragma unroll
     for (int qd = 0; qd < 2; qd++) {
+      u64 acc[7];
 #pragma unroll
       for (int kk = 0; kk < 4; kk++) {
         const float a = stage[(8 * i + 4 * qd + kk) * st];
-        float q[4];
-        q[0] = __fmul_rn(a, y[0]);  // exact: y[0] is a power of two
+        const u64 a2 = pk2(a, a);
+        const float q0 = __fmul_rn(a, y[0]);
+        const u64 q12a = mul2(a2, Y12);
+        const u64 q12 = fma2(fma2(q12a, NU12, a2), Y12, q12a);
+        const float q3a = __fmul_rn(a, y[3]);
+        const float q3 = __fmaf_rn(__fmaf_rn(-q3a, u[3], a), y[3], q3a);
+        float q1, q2;
+        upk2(q12, q1, q2);
+        const u64 QIN[7] = {q12, q12, q12, pk2(q0, q0), pk2(q0, q0), pk2(q3, q3), pk2(q3, q1)};
+        const u64 QSV[7] = {QS_A[0], QS_A[1], QS_A[2], QS_B, QS_C, QS_D, QS_E};
+        const u64 NUV[7] = {NU_A[0], NU_A[1], NU_A[2], NU_B, NU_C, NU_D, NU_E};
 #pragma unroll
-        for (int s = 1; s < 4; s++) {
-          const float q0 = __fmul_rn(a, y[s]);
-          const float r = __fmaf_rn(-q0, u[s], a);
-          q[s] = __fmaf_rn(r, y[s], q0);
-        }
-#pragma unroll
-        for (int idx = 0; idx < 14; idx++) {
-          // unit idx = sig SU * 2^(e0 + MU); SU = 0,0,0,0,1,1,1,1,2,2,2,3,3,3
-          const int s = idx < 4 ? 0 : idx < 8 ? 1 : idx < 11 ? 2 : 3;
-          const int m = idx < 8 ? (idx & 3) : (idx < 11 ? idx - 8 : idx - 11);
-          const float qs = (m == 0) ? 4.0f : (m == 1) ? 2.0f : (m == 2) ? 1.0f : 0.5f;
-          const float uq = __fmul_rn(u[s], (m == 0) ? 0.25f : (m == 1) ? 0.5f : (m == 2) ? 1.0f : 2.0f);
-          const float t = fminf(__fmaf_rn(q[s], qs, kMagic), kMagic + 7.0f);
-          const float mm = __fsub_rn(t, kMagic);
-          const float d = __fmaf_rn(mm, uq, -a);
-          const float e = __fmul_rn(d, d);
-          Q[qd][idx] = kk ? __fadd_rn(Q[qd][idx], e) : e;
+        for (int pi = 0; pi < 7; pi++) {
+          float tl, th;
+          upk2(fma2(QIN[pi], QSV[pi], MAG2), tl, th);
+          const u64 t2 = pk2(fminf(tl, M7), fminf(th, M7));
+          const u64 mm = add2(t2, NMAG2);
+          const u64 d = fma2(mm, NUV[pi], a2);
+          const u64 e = mul2(d, d);
+          acc[pi] = kk ? add2(acc[pi], e) : e;
         }
       }
+      // unit index = 4*s + m for s <= 1, 8 + m for s = 2, 11 + m for s = 3
+      upk2(acc[0], Q[qd][4], Q[qd][8]);
+      upk2(acc[1], Q[qd][5], Q[qd][9]);
+      upk2(acc[2], Q[qd][6], Q[qd][10]);
+      upk2(acc[3], Q[qd][0], Q[qd][1]);
+      upk2(acc[4], Q[qd][2], Q[qd][3]);
+      upk2(acc[5], Q[qd][11], Q[qd][12]);
+      upk2(acc[6], Q[qd][13], Q[qd][7]);
     }
     const int BASE[6] = {0, 4, 8, 11, 1, 5};
 #pragma unroll
@@ -395,6 +464,7 @@ __device__ __forceinline__ uint32_t e6m2_code(float sf) {
   return ((uint32_t)(E + 48) << 2) | ((b >> 21) & 3u);
 }
 
+template <bool PACKED_ONLY>
 __global__ void __launch_bounds__(kConvThreads) convert_kernel(const ConvParams p) {
   extern __shared__ float smem[];
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -417,7 +487,9 @@ __global__ void __launch_bounds__(kConvThreads) convert_kernel(const ConvParams 
                                                           : __fdiv_rn(x[4 * j + n], sv[n]);
     }
   }
-  if (p.rot_signs != nullptr) rot64_exact(x, __ldg(p.rot_signs + bcol), stage, st);
+  if (p.rot_signs != nullptr)
+    rot64_exact(x, __ldg(p.rot_signs + bcol), stage, st,
+                p.src_kind != HIF4X_SRC_VALUES && p.smooth_mode == HIF4X_SMOOTH_NONE);
   if (p.out_x != nullptr) {
     float4 *o4 = reinterpret_cast<float4 *>(p.out_x) + g * 16;
 #pragma unroll
@@ -440,7 +512,7 @@ __global__ void __launch_bounds__(kConvThreads) convert_kernel(const ConvParams 
   if (p.encode_mode == HIF4X_ENC_SEARCH) {
     const float t = fmaxf(__fdiv_rn(amax, 7.0f), 1e-38f);
     const int e0 = floor_log2_torch(t);
-    enc = (e0 >= -48 && e0 <= 14) ? search_fast(stage, st, e0) : search_generic(stage, st, e0);
+    enc = (e0 >= -48 && e0 <= 14) ? search_fast2(stage, st, e0) : search_generic(stage, st, e0);
   } else if (p.encode_mode == HIF4X_ENC_FAST) {
     enc = encode_fast(stage, st, amax);
   } else {
@@ -468,6 +540,39 @@ __global__ void __launch_bounds__(kConvThreads) convert_kernel(const ConvParams 
       }
     }
     enc.bits = bits;
+  }
+
+  // ---- element pass, packed HiF4 only (searched encode): the mantissa code
+  // is read from the magic-number float's bits (t - 1.5*2^23 is an integer
+  // in 0..7 and t's ulp is 1).
+  if (PACKED_ONLY) {
+    const float sf = enc.sf;
+    const float ysf = __fdiv_rn(1.0f, sf);
+    p.meta[g] = e6m2_code(sf) | ((enc.bits & 0xffu) << 8) | ((enc.bits >> 8) << 16);
+    const uint32_t magic_bits = __float_as_uint(kMagic);
+#pragma unroll 1
+    for (int i = 0; i < 8; i++) {
+      const uint32_t l2 = (enc.bits >> i) & 1u;
+      uint32_t nib = 0;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int el = 8 * i + k;
+        const uint32_t l3 = (enc.bits >> (8 + 2 * i + k / 4)) & 1u;
+        const float a = stage[el * st];
+        const float q0 = __fmul_rn(a, ysf);
+        const float q = __fmaf_rn(__fmaf_rn(-q0, sf, a), ysf, q0);
+        const float qs = __fmul_rn(q, (l2 + l3) == 0 ? 4.0f : ((l2 + l3) == 1 ? 2.0f : 1.0f));
+        uint32_t m4;
+        if (qs < 4194304.0f) {
+          m4 = __float_as_uint(fminf(__fadd_rn(qs, kMagic), kMagic + 7.0f)) - magic_bits;
+        } else {
+          m4 = 7u;
+        }
+        nib |= ((uint32_t)((neg >> el) & 1ull) << 3 | m4) << (4 * k);
+      }
+      reinterpret_cast<uint32_t *>(p.codes)[g * 8 + i] = nib;
+    }
+    return;
   }
 
   // ---- element pass: mant, sign and every requested output
@@ -700,7 +805,7 @@ __global__ void __launch_bounds__(kConvThreads) rotate64_kernel(const float *x, 
     const float4 a = __ldg(x4 + j);
     v[4 * j] = a.x; v[4 * j + 1] = a.y; v[4 * j + 2] = a.z; v[4 * j + 3] = a.w;
   }
-  rot64_exact(v, __ldg(signs + g % nb), smem + threadIdx.x, blockDim.x);
+  rot64_exact(v, __ldg(signs + g % nb), smem + threadIdx.x, blockDim.x, false);
   float4 *o4 = reinterpret_cast<float4 *>(out) + g * 16;
 #pragma unroll
   for (int j = 0; j < 16; j++) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
@@ -740,7 +845,12 @@ extern "C" int hif4x_convert(const hif4x_convert_desc *d, void *stream) {
   p.sf = d->sf; p.lv2 = d->lv2; p.lv3 = d->lv3; p.sign = d->sign; p.mant = d->mant;
   p.meta = d->meta; p.codes = d->codes; p.deq = d->deq; p.deq_dtype = d->deq_dtype; p.unit = d->unit;
   const size_t smem = 64 * kConvThreads * sizeof(float);
-  convert_kernel<<<nblocks(p.ngroups, kConvThreads), kConvThreads, smem, (cudaStream_t)stream>>>(p);
+  const bool packed_only = d->encode_mode == HIF4X_ENC_SEARCH && d->meta && d->codes && !d->out_x && !d->sf &&
+                           !d->lv2 && !d->lv3 && !d->sign && !d->mant && !d->deq && !d->unit;
+  if (packed_only)
+    convert_kernel<true><<<nblocks(p.ngroups, kConvThreads), kConvThreads, smem, (cudaStream_t)stream>>>(p);
+  else
+    convert_kernel<false><<<nblocks(p.ngroups, kConvThreads), kConvThreads, smem, (cudaStream_t)stream>>>(p);
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
 }

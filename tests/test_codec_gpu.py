@@ -176,3 +176,13 @@ def test_c1_full_size_row_sample():
     xr = codec.rotate64(dec)
     rel = ((rt.float() - xr) ** 2).sum() / (xr ** 2).sum()
     assert 0 < float(rel) < 0.02
+
+
+def test_packed_only_path_edges(codec_golden):
+    """Packed-only outputs (the codec hot path) on the edge-case rows: meta and
+    codes equal the reference dict5 packed by the oracle."""
+    g = codec_golden
+    out = codec.convert(cuda(g["enc_in"]), kind=L.SRC_VALUES, dict5=False, packed=True)
+    meta_o, codes_o = oracle.pack_hif4(dict5_from_golden(g, "enc_"))
+    np.testing.assert_array_equal(out["meta"].cpu().numpy().view(np.uint32), meta_o)
+    np.testing.assert_array_equal(out["codes"].cpu().numpy(), codes_o)
