@@ -26,6 +26,7 @@
 namespace hif4x {
 
 constexpr int kConvThreads = 128;
+__device__ __constant__ float kE2M1[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
 
 struct ConvParams {
   int64_t ngroups, nb;
@@ -61,15 +62,37 @@ __device__ __forceinline__ void load_group(const ConvParams &p, int64_t g, float
     const uint4 *c4 = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.src) + g * 32);
     const uint4 v0 = __ldcs(c4), v1 = __ldcs(c4 + 1);
     const uint32_t sc = __ldcs(reinterpret_cast<const unsigned int *>(p.src_scale) + g);
-    float s[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) s[k] = __fmul_rn(e4m3_to_f32((sc >> (8 * k)) & 0xffu), p.s_dec);
     const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-    for (int j = 0; j < 8; j++)
+    for (int k = 0; k < 4; k++) {
+      // the 8 magnitudes of this 16-element block, bf16(E2M1[i] * s), as byte
+      // tables: H = high bytes, Lo = low bytes of the bf16 patterns (i = 0..7)
+      const float sk = __fmul_rn(e4m3_to_f32((sc >> (8 * k)) & 0xffu), p.s_dec);
+      uint32_t W[4];
 #pragma unroll
-      for (int n = 0; n < 8; n++)
-        x[8 * j + n] = bf16_round(__fmul_rn(e2m1_to_f32((w[j] >> (4 * n)) & 15u), s[j >> 1]));
+      for (int i = 0; i < 4; i++) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(__fmul_rn(kE2M1[2 * i], sk), __fmul_rn(kE2M1[2 * i + 1], sk));
+        W[i] = *reinterpret_cast<const uint32_t *>(&b2);
+      }
+      const uint32_t Hlo = __byte_perm(W[0], W[1], 0x7531), Hhi = __byte_perm(W[2], W[3], 0x7531);
+      const uint32_t Llo = __byte_perm(W[0], W[1], 0x6420), Lhi = __byte_perm(W[2], W[3], 0x6420);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {           // two code words per 16-element block
+        const uint32_t cw = w[2 * k + h];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {         // 4 elements per lookup
+          const uint32_t sel = (cw >> (16 * q)) & 0x7777u;
+          const uint32_t hi4 = __byte_perm(Hlo, Hhi, sel), lo4 = __byte_perm(Llo, Lhi, sel);
+          const uint32_t p01 = __byte_perm(lo4, hi4, 0x5140), p23 = __byte_perm(lo4, hi4, 0x7362);
+          const uint32_t bf[4] = {p01 << 16, p01 & 0xffff0000u, p23 << 16, p23 & 0xffff0000u};
+#pragma unroll
+          for (int n = 0; n < 4; n++) {
+            const int j = 4 * q + n;            // nibble j of cw carries its sign in bit 4j+3
+            x[16 * k + 8 * h + j] = __uint_as_float(bf[n] | ((cw << (28 - 4 * j)) & 0x80000000u));
+          }
+        }
+      }
+    }
     return;
   }
   if (p.src_kind == HIF4X_SRC_NVFP4_PAIR) {
@@ -293,7 +316,8 @@ __device__ __forceinline__ Enc search_fast2(const float *stage, int st, int e0) 
         for (int pi = 0; pi < 7; pi++) {
           float tl, th;
           upk2(fma2(QIN[pi], QSV[pi], MAG2), tl, th);
-          const u64 t2 = pk2(fminf(tl, M7), fminf(th, M7));
+          // scales m = 3 never round above 7 (q < 14): C.hi = (0,3), E.hi = (1,3) skip the clamp
+          const u64 t2 = pk2(fminf(tl, M7), (pi == 4 || pi == 6) ? th : fminf(th, M7));
           const u64 mm = add2(t2, NMAG2);
           const u64 d = fma2(mm, NUV[pi], a2);
           const u64 e = mul2(d, d);
