@@ -489,7 +489,7 @@ __device__ __forceinline__ uint32_t e6m2_code(float sf) {
 }
 
 template <bool PACKED_ONLY>
-__global__ void __launch_bounds__(kConvThreads) convert_kernel(const ConvParams p) {
+__global__ void __launch_bounds__(kConvThreads, 5) convert_kernel(const ConvParams p) {
   extern __shared__ float smem[];
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= p.ngroups) return;
