@@ -128,8 +128,11 @@ def _refine_weight_values(w_final, q_used, weight_params: Dict5, calib_sm, mode)
 
 
 def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, calib_activation_list: list,
-                     info: dict | None = None) -> dict[str, Any]:
-    """hif4_calibration_and_quantize_weight (solution.py:826-1026)."""
+                     info: dict | None = None, return_device: bool = False) -> dict[str, Any]:
+    """hif4_calibration_and_quantize_weight (solution.py:826-1026).
+
+    return_device=True keeps the weight parameters and the state tensors on the
+    GPU (for device-resident pipelines); the API form returns CPU tensors."""
     torch.manual_seed(0)                                       # solution.py:838
     dev = _dev()
     ph = _Phases(info is not None)
@@ -267,17 +270,18 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         info.update(alpha=best_alpha, mode=mode, gptq_w=gptq_w, gptq_act=gptq_act, e3=refined, tmax=tmax,
                     w_final=w_final, q_used=q_used, s=s)
     la.check_device_status(dev)
+    out = (lambda t: t) if return_device else (lambda t: t.cpu().contiguous())
     activation_state = {
-        "s": s.cpu().contiguous(),
+        "s": out(s),
         "mode": mode,
-        "u_act": u_act.cpu().contiguous() if u_act is not None else None,
+        "u_act": out(u_act) if u_act is not None else None,
         "g": gptq_act,
-        "order": order.cpu().contiguous() if (gptq_act == 1 and order is not None) else None,
-        "gw": gw.cpu() if gw is not None else None,
-        "gwf": gwf.cpu() if gwf is not None else None,
+        "order": out(order) if (gptq_act == 1 and order is not None) else None,
+        "gw": out(gw) if gw is not None else None,
+        "gwf": out(gwf) if gwf is not None else None,
         "tmax": tmax,
     }
-    return {"weight_params": weight_params.reference(), "activation_state": activation_state}
+    return {"weight_params": weight_params.reference(cpu=not return_device), "activation_state": activation_state}
 
 
 def refine_act_values(x, values, unit, gw, gwf) -> torch.Tensor:
