@@ -2,24 +2,31 @@
 //
 //   C = alpha * op(A) op(B) + beta * C,  fp32 in / fp32 out, row-major.
 //
-// Each fp32 operand x is split in shared memory into x_hi = x with the low 13
-// mantissa bits cleared (an exact TF32 value) and x_lo = x - x_hi (exact in
-// fp32); the tile product is accumulated as hi*hi + hi*lo + lo*hi by
-// tcgen05.mma kind::tf32 into fp32 accumulators in tensor memory, which keeps
-// ~21 significant bits per product (the dropped lo*lo term is < 2^-20 of it).
+// Each fp32 operand x is split once, in a pass over global memory, into
+// x_hi = x with the low 13 mantissa bits cleared (an exact TF32 value) and
+// x_lo = x - x_hi (exact in fp32), written K-contiguous whatever the
+// operand's storage order; the product is accumulated as hi*hi + hi*lo +
+// lo*hi by tcgen05.mma kind::tf32 into fp32 accumulators in tensor memory,
+// which keeps ~21 significant bits per product (the dropped lo*lo term is
+// < 2^-20 of it).  Splitting outside the GEMM keeps shared memory for the
+// TMA writes and the tensor core's operand reads alone: an in-kernel split
+// made the conversion's loads/stores and the MMA operand reads compete for
+// the shared-memory banks and capped the tensor pipe near 40 %.
 //
-// CTA tile 128 x 128, K step 32, 3-stage pipeline, 192 threads:
+// Persistent kernel, one CTA per SM, 128 x 128 output tiles visited in
+// bands of GROUP tile-rows (column by column within a band) so that the CTAs
+// running at one time share A and B panels in L2.  192 threads:
 //   warp 0   TMA producer (one lane) + tensor-memory allocation (whole warp)
 //   warp 1   MMA issuer (one lane): 4 K-substeps x 3 products per stage
-//   warps 2-5 split fp32 tiles into hi/lo, then the epilogue (tcgen05.ld of
-//            their TMEM lane quarter -> alpha/beta -> global)
-// Operands are TMA-loaded with 128-byte swizzle either K-major (K contiguous:
-// one 128 x 32 box) or MN-major (M/N contiguous: four 32 x 32 boxes), matching
-// the UMMA shared-memory descriptors below.  Every mbarrier wait is bounded:
-// on expiry the kernel records HIF4X_TIMEOUT in a device status word and
-// finishes without further waits; hif4x_device_status() reports it.
+//   warps 2-5 epilogue: tcgen05.ld of their TMEM lane quarter -> alpha/beta
+//            -> global, on one of two accumulator buffers while the MMA
+//            warp fills the other
+// Every mbarrier wait is bounded: on expiry the kernel records
+// HIF4X_TIMEOUT in a device status word and finishes without further
+// waits; hif4x_device_status() reports it.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -32,7 +39,8 @@ constexpr int TILE_BYTES = BM * BK * 4;           // 16 KiB (A and B tiles are t
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;        // A hi, A lo, B hi, B lo
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* align */ + 256 /* barriers */;
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 128;
+constexpr uint32_t TMEM_COLS = 2 * BN;            // two accumulator buffers of BN fp32 columns
+constexpr int GROUP = 8;                          // tile-rows per rasterisation band
 constexpr long long SPIN_LIMIT = 1ll << 22;
 
 __device__ int g_status;   // sticky device status: 0 or HIF4X_TIMEOUT
@@ -111,34 +119,64 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                : "memory");
 }
 
+// K-major operand descriptor of K-substep j (8 K-elements) of a 128 x 32
+// tile: rows of 128 B (32 K values), 8-row swizzle groups 1 KiB apart; a
+// substep moves 32 B along the row.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int j) {
+  return smem_desc(base + 32u * j, 16u, 1024u, 2u);
+}
+
 struct TcArgs {
   int64_t M, N, K;
   float alpha, beta;
   float *C;
   int64_t ldc;
-  int a_mn, b_mn;   // operand majors: 1 = M/N contiguous in global (and smem)
-  int lower;        // 1: only tiles touching the lower triangle (n0 <= m0 + BM - 1)
+  int a_lo, b_lo;   // row of the lo half in each split operand (hi rows come first)
+  int tm, tn;       // tile rows / columns
+  int lower;        // 1: only tiles on or below the diagonal (square C)
+  int vec;          // 1: C rows take 16-byte stores
+  int64_t ntiles;
 };
 
-// operand tile loads for one stage (K-major: one 128x32 box; MN-major: four 32x32 boxes)
-__device__ __forceinline__ void load_operand(const CUtensorMap *map, int mn_major, uint8_t *dst, uint64_t *bar,
-                                             int mn0, int k0) {
-  if (!mn_major) {
-    tma_load_2d(map, dst, bar, k0, mn0);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; i++) tma_load_2d(map, dst + i * 4096, bar, mn0 + 32 * i, k0);
+// Tile t of the visiting order -> (tile row, tile column).  Bands of GROUP
+// tile-rows; inside a band, column by column.  With `lower` (tm == tn) only
+// tiles with column <= row exist: band b holds rows [bG, bG+g), each row i
+// with columns 0..i, so the band is a g-wide rectangle of bG columns followed
+// by a g-row triangle.
+__device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &ti, int &tj) {
+  if (!a.lower) {
+    const int64_t per_band = (int64_t)GROUP * a.tn;
+    const int band = (int)(t / per_band);
+    const int64_t r = t - band * per_band;
+    const int g = min(GROUP, a.tm - band * GROUP);
+    tj = (int)(r / g);
+    ti = band * GROUP + (int)(r % g);
+    return;
   }
-}
-
-// descriptor of K-substep j (8 K-elements) of an operand tile.
-// K-major: rows of 128 B (32 K values), 8-row groups 1 KiB apart; a substep
-// moves 32 B along the row.  MN-major: per 32-element MN atom (one 4 KiB TMA
-// box, LBO apart) K-rows of 128 B, 4-row swizzle groups 512 B apart (SBO); a
-// substep moves 8 K-rows = 1 KiB.
-__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int j) {
-  if (!mn_major) return smem_desc(base + 32u * j, 16u, 1024u, 2u);
-  return smem_desc(base + 1024u * j, 4096u, 512u, 1u);
+  int band = 0;
+  int64_t start = 0;
+  for (;;) {
+    const int r0 = band * GROUP, g = min(GROUP, a.tm - r0);
+    const int64_t size = (int64_t)g * r0 + (int64_t)g * (g + 1) / 2;
+    if (t < start + size) break;
+    start += size;
+    band++;
+  }
+  const int r0 = band * GROUP, g = min(GROUP, a.tm - r0);
+  int64_t u = t - start;
+  if (u < (int64_t)r0 * g) {
+    tj = (int)(u / g);
+    ti = r0 + (int)(u % g);
+    return;
+  }
+  u -= (int64_t)r0 * g;
+  int jj = 0;
+  while (u >= g - jj) {
+    u -= g - jj;
+    jj++;
+  }
+  tj = r0 + jj;
+  ti = r0 + jj + (int)u;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
@@ -147,23 +185,25 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-  uint64_t *conv = full + STAGES;
-  uint64_t *empty = conv + STAGES;
-  uint64_t *accum = empty + STAGES;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;   // [2] accumulator buffer complete
+  uint64_t *tempty = tfull + 2;       // [2] accumulator buffer drained by the epilogue
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int nk = (int)((args.K + BK - 1) / BK);
-  if (args.lower && n0 > m0 + BM - 1) return;   // tile strictly above the diagonal: nothing to do
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 128);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -179,105 +219,134 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   bool ok = true;
 
   if (warp == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer: hi and lo tiles of A and B per stage
     if (lane == 0) {
-      int issued_last[STAGES] = {-1, -1, -1};
-      for (int kt = 0; kt < nk && ok; kt++) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES) ok = mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1);
-        if (!ok) break;
-        uint8_t *st = smem + s * STAGE_BYTES;
-        mbar_expect_tx(&full[s], 2 * TILE_BYTES);
-        load_operand(&mapA, args.a_mn, st, &full[s], m0, kt * BK);
-        load_operand(&mapB, args.b_mn, st + 2 * TILE_BYTES, &full[s], n0, kt * BK);
-        issued_last[s] = kt;
+      int64_t g = 0;   // stage fills issued so far (a failed wait leaves g unissued)
+      for (int64_t t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
+        int ti, tj;
+        tile_coords(args, t, ti, tj);
+        const int m0 = ti * BM, n0 = tj * BN;
+        for (int kt = 0; kt < nk; kt++, g++) {
+          const int s = (int)(g % STAGES);
+          if (g >= STAGES) ok = mbar_wait(&empty[s], (uint32_t)(((g / STAGES) - 1) & 1));
+          if (!ok) break;
+          uint8_t *st = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(&mapA, st, &full[s], kt * BK, m0);
+          tma_load_2d(&mapA, st + TILE_BYTES, &full[s], kt * BK, args.a_lo + m0);
+          tma_load_2d(&mapB, st + 2 * TILE_BYTES, &full[s], kt * BK, n0);
+          tma_load_2d(&mapB, st + 3 * TILE_BYTES, &full[s], kt * BK, args.b_lo + n0);
+        }
       }
-      // drain: every issued copy has landed before the CTA may exit
+      // drain: every issued copy has landed before the CTA may exit (the
+      // last fill of stage s is the largest g' < g with g' % STAGES == s)
+#pragma unroll
       for (int s = 0; s < STAGES; s++)
-        if (issued_last[s] >= 0) mbar_wait(&full[s], (issued_last[s] / STAGES) & 1);
+        if (g > s) mbar_wait(&full[s], (uint32_t)(((s + STAGES * ((g - 1 - s) / STAGES)) / STAGES) & 1));
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(args.a_mn, args.b_mn);
-      for (int kt = 0; kt < nk && ok; kt++) {
-        const int s = kt % STAGES;
-        ok = mbar_wait(&conv[s], (kt / STAGES) & 1);
+      const uint32_t idesc = instr_desc(0, 0);
+      int64_t g = 0;
+      int lt = 0;
+      for (int64_t t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x, lt++) {
+        const int buf = lt & 1, use = lt >> 1;
+        if (use > 0) ok = mbar_wait(&tempty[buf], (uint32_t)((use - 1) & 1));
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t a_hi = base, a_lo = base + TILE_BYTES;
-        const uint32_t b_hi = base + 2 * TILE_BYTES, b_lo = base + 3 * TILE_BYTES;
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kt = 0; kt < nk; kt++, g++) {
+          const int s = (int)(g % STAGES);
+          ok = mbar_wait(&full[s], (uint32_t)((g / STAGES) & 1));
+          if (!ok) break;
+          asm volatile("tcgen05.fence::after_thread_sync;");
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t a_hi = base, a_lo = base + TILE_BYTES;
+          const uint32_t b_hi = base + 2 * TILE_BYTES, b_lo = base + 3 * TILE_BYTES;
 #pragma unroll
-        for (int j = 0; j < BK / 8; j++) {
-          const uint64_t dah = operand_desc(a_hi, args.a_mn, j), dal = operand_desc(a_lo, args.a_mn, j);
-          const uint64_t dbh = operand_desc(b_hi, args.b_mn, j), dbl = operand_desc(b_lo, args.b_mn, j);
-          mma_tf32(tmem, dah, dbh, idesc, (kt > 0 || j > 0) ? 1u : 0u);
-          mma_tf32(tmem, dah, dbl, idesc, 1u);
-          mma_tf32(tmem, dal, dbh, idesc, 1u);
+          for (int j = 0; j < BK / 8; j++) {
+            const uint64_t dah = kmajor_desc(a_hi, j), dal = kmajor_desc(a_lo, j);
+            const uint64_t dbh = kmajor_desc(b_hi, j), dbl = kmajor_desc(b_lo, j);
+            mma_tf32(d, dah, dbh, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+            mma_tf32(d, dah, dbl, idesc, 1u);
+            mma_tf32(d, dal, dbh, idesc, 1u);
+          }
+          mma_commit(&empty[s]);   // stage s free once these MMAs have read it
         }
-        mma_commit(&empty[s]);   // stage s free once these MMAs have read it
+        if (!ok) break;
+        mma_commit(&tfull[buf]);   // accumulator buffer complete
       }
-      mma_commit(accum);         // accumulators complete
+      // every issued MMA has finished before tensor memory is released
+      mma_commit(drain);
+      mbar_wait(drain, 0);
     }
   } else {
-    // ---------------- split fp32 -> tf32 hi + lo (threads 64..191)
-    const int t = threadIdx.x - 64;
-    for (int kt = 0; kt < nk && ok; kt++) {
-      const int s = kt % STAGES;
-      ok = mbar_wait(&full[s], (kt / STAGES) & 1);
+    // ---------------- epilogue (threads 64..191): TMEM lane quarter (warp % 4) -> rows
+    const int quarter = warp & 3;
+    int lt = 0;
+    for (int64_t t = blockIdx.x; t < args.ntiles; t += gridDim.x, lt++) {
+      const int buf = lt & 1, use = lt >> 1;
+      ok = mbar_wait(&tfull[buf], (uint32_t)(use & 1));
+      ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld below is warp-collective
       if (!ok) break;
-      uint8_t *st = smem + s * STAGE_BYTES;
-#pragma unroll
-      for (int op = 0; op < 2; op++) {
-        float4 *hi = reinterpret_cast<float4 *>(st + op * 2 * TILE_BYTES);
-        float4 *lo = reinterpret_cast<float4 *>(st + op * 2 * TILE_BYTES + TILE_BYTES);
-#pragma unroll
-        for (int i = 0; i < TILE_BYTES / 16 / 128; i++) {
-          const int e = t + 128 * i;
-          float4 v = hi[e];
-          float4 h, l;
-          h.x = __uint_as_float(__float_as_uint(v.x) & 0xffffe000u); l.x = __fsub_rn(v.x, h.x);
-          h.y = __uint_as_float(__float_as_uint(v.y) & 0xffffe000u); l.y = __fsub_rn(v.y, h.y);
-          h.z = __uint_as_float(__float_as_uint(v.z) & 0xffffe000u); l.z = __fsub_rn(v.z, h.z);
-          h.w = __uint_as_float(__float_as_uint(v.w) & 0xffffe000u); l.w = __fsub_rn(v.w, h.w);
-          hi[e] = h;
-          lo[e] = l;
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&conv[s]);
-    }
-    // ---------------- epilogue: TMEM lane quarter (warp % 4) -> rows
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) ok = mbar_wait(accum, 0);
-    ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld below is warp-collective
-    if (ok) {
       asm volatile("tcgen05.fence::after_thread_sync;");
-      const int quarter = warp & 3;
-      const int64_t row = (int64_t)m0 + quarter * 32 + lane;
-#pragma unroll 1
+      int ti, tj;
+      tile_coords(args, t, ti, tj);
+      const int64_t row = (int64_t)ti * BM + quarter * 32 + lane;
+      const int64_t n0 = (int64_t)tj * BN;
+      uint32_t r[BN];
+#pragma unroll
       for (int c = 0; c < BN / 32; c++) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32);
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c * 32);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
             "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
-              "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-              "=r"(r[30]), "=r"(r[31])
+            : "=r"(r[c * 32 + 0]), "=r"(r[c * 32 + 1]), "=r"(r[c * 32 + 2]), "=r"(r[c * 32 + 3]),
+              "=r"(r[c * 32 + 4]), "=r"(r[c * 32 + 5]), "=r"(r[c * 32 + 6]), "=r"(r[c * 32 + 7]),
+              "=r"(r[c * 32 + 8]), "=r"(r[c * 32 + 9]), "=r"(r[c * 32 + 10]), "=r"(r[c * 32 + 11]),
+              "=r"(r[c * 32 + 12]), "=r"(r[c * 32 + 13]), "=r"(r[c * 32 + 14]), "=r"(r[c * 32 + 15]),
+              "=r"(r[c * 32 + 16]), "=r"(r[c * 32 + 17]), "=r"(r[c * 32 + 18]), "=r"(r[c * 32 + 19]),
+              "=r"(r[c * 32 + 20]), "=r"(r[c * 32 + 21]), "=r"(r[c * 32 + 22]), "=r"(r[c * 32 + 23]),
+              "=r"(r[c * 32 + 24]), "=r"(r[c * 32 + 25]), "=r"(r[c * 32 + 26]), "=r"(r[c * 32 + 27]),
+              "=r"(r[c * 32 + 28]), "=r"(r[c * 32 + 29]), "=r"(r[c * 32 + 30]), "=r"(r[c * 32 + 31])
             : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row < args.M) {
-          float *crow = args.C + row * args.ldc;
+      }
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      // the buffer's values are in registers: hand it back to the MMA warp
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      mbar_arrive(&tempty[buf]);
+      if (row < args.M) {
+        float *crow = args.C + row * args.ldc;
+        const float alpha = args.alpha, beta = args.beta;
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int64_t col = (int64_t)n0 + c * 32 + j;
-            if (col < args.N) {
-              const float v = args.alpha * __uint_as_float(r[j]);
-              crow[col] = args.beta == 0.0f ? v : fmaf(args.beta, crow[col], v);
+        for (int c = 0; c < BN / 32; c++) {
+          const int64_t col0 = n0 + c * 32;
+          if (args.vec && col0 + 32 <= args.N) {
+            float4 *dst = reinterpret_cast<float4 *>(crow + col0);
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+              float4 v = make_float4(alpha * __uint_as_float(r[c * 32 + 4 * q + 0]),
+                                     alpha * __uint_as_float(r[c * 32 + 4 * q + 1]),
+                                     alpha * __uint_as_float(r[c * 32 + 4 * q + 2]),
+                                     alpha * __uint_as_float(r[c * 32 + 4 * q + 3]));
+              if (beta != 0.0f) {
+                const float4 o = dst[q];
+                v.x = fmaf(beta, o.x, v.x);
+                v.y = fmaf(beta, o.y, v.y);
+                v.z = fmaf(beta, o.z, v.z);
+                v.w = fmaf(beta, o.w, v.w);
+              }
+              dst[q] = v;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              const int64_t col = col0 + j;
+              if (col < args.N) {
+                const float v = alpha * __uint_as_float(r[c * 32 + j]);
+                crow[col] = beta == 0.0f ? v : fmaf(beta, crow[col], v);
+              }
             }
           }
         }
@@ -290,6 +359,36 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// Split an operand into TF32 hi / lo halves, K-contiguous:
+//   dst[r * kp + k] = hi(x(r, k)),  dst[(R + r) * kp + k] = lo(x(r, k))
+// where x(r, k) = src[r * ld + k] (k_contig) or src[k * ld + r].  32 x 32
+// tiles; the transposing form goes through shared memory so that both the
+// loads and the stores are coalesced.
+__global__ void split_tf32_kernel(const float *__restrict__ src, int64_t ld, int k_contig, int64_t R, int64_t K,
+                                  float *__restrict__ dst, int64_t kp) {
+  __shared__ float tile[32][33];
+  const int64_t k0 = (int64_t)blockIdx.x * 32, r0 = (int64_t)blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
+  if (!k_contig) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int64_t k = k0 + ty + 8 * i, r = r0 + tx;
+      tile[ty + 8 * i][tx] = (k < K && r < R) ? src[k * ld + r] : 0.0f;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int64_t r = r0 + ty + 8 * i, k = k0 + tx;
+    if (r < R && k < K) {
+      const float x = k_contig ? src[r * ld + k] : tile[tx][ty + 8 * i];
+      const float hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+      dst[r * kp + k] = hi;
+      dst[(R + r) * kp + k] = __fsub_rn(x, hi);
+    }
   }
 }
 
@@ -311,18 +410,50 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D fp32 tensor map: inner dim (contiguous) x outer dim, row stride ld floats.
-static bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld, int box_inner,
-                     int box_outer, CUtensorMapSwizzle swz) {
+// 2-D fp32 tensor map over a split operand: `inner` (K) x `outer` (2R) floats,
+// row stride ld floats, 32 x 128 boxes, 128-byte swizzle; K beyond `inner`
+// reads as zero.
+static bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kMaxDevices = 64;
+
+// Per device: SM count, and the stream-ordered pool the split operands come
+// from set to keep its memory between calls (the split buffers are
+// allocated and freed around every product).
+static int device_sms(int dev) {
+  static int sms[kMaxDevices];
+  static std::once_flag once[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return 0;
+  std::call_once(once[dev], [dev] {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 0;
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    sms[dev] = n;
+  });
+  return sms[dev];
+}
+
+static int split_operand(const float *src, int64_t ld, int k_contig, int64_t R, int64_t K, float *dst, int64_t kp,
+                         cudaStream_t s) {
+  const int64_t gy = (R + 31) / 32;
+  if (gy > 65535) return HIF4X_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)((K + 31) / 32), (unsigned)gy);
+  split_tf32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, k_contig, R, K, dst, kp);
+  return HIF4X_OK;
 }
 
 }  // namespace tc
@@ -330,10 +461,6 @@ static bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t
 
 using namespace hif4x;
 
-// Tensor-core path of hif4x_gemm (batch 1).  Returns HIF4X_ERR_UNSUPPORTED
-// when the operands do not meet the TMA rules (16-byte aligned bases,
-// leading dimensions a multiple of 4 floats), so the caller can take the
-// SIMT kernel instead.
 int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
                      const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream);
 
@@ -343,29 +470,63 @@ extern "C" int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, fl
   return hif4x_gemm_tc_ex(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, 0, stream);
 }
 
-// Same, optionally restricted to output tiles that touch the lower triangle.
+// Same, optionally restricted to output tiles on or below the diagonal
+// (lower != 0 and M == N; a diagonal tile is written whole).  The split
+// operands live in a stream-ordered allocation of 2 * kp * (M + N) floats
+// (2 * kp * M when A and B are the same operand, as in X^T X or L L^T).
+// Returns HIF4X_ERR_UNSUPPORTED when a tensor map cannot be built, so the
+// caller can take the SIMT kernel instead.
 int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
                      const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return HIF4X_ERR_ARG;
-  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (!al16(A) || !al16(B) || (lda & 3) || (ldb & 3)) return HIF4X_ERR_UNSUPPORTED;
-  if ((M + tc::BM - 1) / tc::BM > 65535) return HIF4X_ERR_UNSUPPORTED;
+  cudaStream_t s = (cudaStream_t)stream;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+  const int sms = tc::device_sms(dev);
+  if (sms <= 0) return HIF4X_ERR_LAUNCH;
+  const int64_t kp = (K + 3) / 4 * 4;   // 16-byte row pitch for the tensor maps
+  // operand (r, k) is K-contiguous in memory for A when ta == 0 and for B when tb == 1
+  const int a_kc = ta ? 0 : 1, b_kc = tb ? 1 : 0;
+  const bool same = A == B && lda == ldb && a_kc == b_kc && M == N;
+  if (2 * (M + N) > INT32_MAX) return HIF4X_ERR_UNSUPPORTED;   // TMA row coordinates are 32-bit
+  const int64_t a_floats = 2 * kp * M, b_floats = same ? 0 : 2 * kp * N;
+  float *ws = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void **>(&ws), (size_t)(a_floats + b_floats) * sizeof(float), s) !=
+      cudaSuccess)
+    return HIF4X_ERR_LAUNCH;
+  float *As = ws, *Bs = same ? ws : ws + a_floats;
+  int st = tc::split_operand(A, lda, a_kc, M, K, As, kp, s);
+  if (st == HIF4X_OK && !same) st = tc::split_operand(B, ldb, b_kc, N, K, Bs, kp, s);
   CUtensorMap ma, mb;
-  // A: ta = 0 -> stored M x K (K contiguous, K-major); ta = 1 -> stored K x M (MN-major)
-  const CUtensorMapSwizzle KSW = CU_TENSOR_MAP_SWIZZLE_128B, MNSW = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-  const bool okA = ta ? tc::make_map(&ma, A, M, K, lda, 32, 32, MNSW) : tc::make_map(&ma, A, K, M, lda, 32, 128, KSW);
-  // B: tb = 1 -> stored N x K (K-major); tb = 0 -> stored K x N (MN-major)
-  const bool okB = tb ? tc::make_map(&mb, B, K, N, ldb, 32, 128, KSW) : tc::make_map(&mb, B, N, K, ldb, 32, 32, MNSW);
-  if (!okA || !okB) return HIF4X_ERR_UNSUPPORTED;
-  tc::TcArgs args{M, N, K, alpha, beta, C, ldc, ta ? 1 : 0, tb ? 0 : 1, lower ? 1 : 0};
-  static std::once_flag attr_once;
-  std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(tc::gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
-  });
-  dim3 grid((unsigned)((N + tc::BN - 1) / tc::BN), (unsigned)((M + tc::BM - 1) / tc::BM));
-  tc::gemm_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, (cudaStream_t)stream>>>(ma, mb, args);
-  HIF4X_CHECK_LAUNCH();
-  return HIF4X_OK;
+  if (st == HIF4X_OK && (!tc::make_map(&ma, As, K, 2 * M, kp) || !tc::make_map(&mb, Bs, K, 2 * N, kp)))
+    st = HIF4X_ERR_UNSUPPORTED;
+  if (st == HIF4X_OK) {
+    tc::TcArgs args{};
+    args.M = M;
+    args.N = N;
+    args.K = K;
+    args.alpha = alpha;
+    args.beta = beta;
+    args.C = C;
+    args.ldc = ldc;
+    args.a_lo = (int)M;
+    args.b_lo = (int)N;
+    args.tm = (int)((M + tc::BM - 1) / tc::BM);
+    args.tn = (int)((N + tc::BN - 1) / tc::BN);
+    args.lower = (lower && M == N) ? 1 : 0;
+    args.vec = ((ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0) ? 1 : 0;
+    args.ntiles = args.lower ? (int64_t)args.tm * (args.tm + 1) / 2 : (int64_t)args.tm * args.tn;
+    static std::once_flag attr_once;
+    std::call_once(attr_once, [] {
+      cudaFuncSetAttribute(tc::gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+    });
+    const int64_t grid = std::min<int64_t>(args.ntiles, sms);
+    tc::gemm_tc_kernel<<<(unsigned)grid, tc::THREADS, tc::SMEM_BYTES, s>>>(ma, mb, args);
+  }
+  const cudaError_t launch = cudaGetLastError();
+  cudaFreeAsync(ws, s);
+  if (st != HIF4X_OK) return st;
+  return launch == cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
 }
 
 // Synchronises the stream and reports (then clears) the sticky device status

@@ -45,3 +45,41 @@ def test_tc_gemm_alpha_beta():
     ref = -1.0 * (A.double() @ B.double()) + 1.0 * C.double()
     got = tc_gemm(A, B, 0, 0, alpha=-1.0, beta=1.0, C=C.clone())
     assert float((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * 512 ** 0.5 + 1e-6
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 2560, 256), (1100, 2000, 300)])
+def test_tc_gemm_many_tiles_per_cta(M, N, K):
+    """More output tiles than SMs: each persistent CTA runs several tiles and
+    alternates its two accumulator buffers."""
+    A, B = rnd(M, K, seed=6), rnd(N, K, seed=7)
+    ref = A.double() @ B.double().T
+    got = tc_gemm(A, B, 0, 1)
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    assert float((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * K ** 0.5 + 1e-6
+
+
+def test_tc_gemm_shared_operand_gram():
+    """X^T X with A and B the same buffer (split once).  C[i, j] and C[j, i]
+    sum the hi*lo and lo*hi terms in different orders, so the result is
+    symmetric to rounding, not bit for bit."""
+    X = rnd(700, 1000, seed=8)
+    ref = X.double().T @ X.double()
+    got = tc_gemm(X, X, 1, 0)
+    assert float((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * 700 ** 0.5 + 1e-6
+    assert float((got - got.T).abs().max() / got.abs().max()) < 1e-6
+
+
+def test_tc_gemm_unaligned_leading_dims():
+    """Leading dimensions that are not a multiple of 4 floats and a C that is
+    not 16-byte aligned (scalar epilogue)."""
+    Abig, Bbig = rnd(200, 301, seed=9), rnd(301, 259, seed=10)
+    A, B = Abig[:, :299], Bbig[:299, :257]
+    Cbig = torch.zeros(200, 262, device="cuda")
+    C = Cbig[:, 1:258]
+    M, K, N = 200, 299, 257
+    st = L.call("hif4x_gemm_tc", 0, 0, M, N, K, L.f32(1.0), L.ptr(A), 301, L.ptr(B), 259, L.f32(0.0), L.ptr(C), 262,
+                L.stream())
+    assert st == L.OK
+    ref = A.double() @ B.double()
+    assert float((C.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * K ** 0.5 + 1e-6
+    assert float(Cbig[:, 0].abs().max()) == 0.0 and float(Cbig[:, 258:].abs().max()) == 0.0
