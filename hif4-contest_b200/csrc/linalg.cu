@@ -145,6 +145,84 @@ __global__ void __launch_bounds__(GTHREADS) gemm_kernel(const GemmArgs g) {
   }
 }
 
+// Small products: 32 x 32 output tiles so that a 128-sized product still
+// spreads over 16 SMs, K in chunks of 64 (one global-memory round trip per
+// chunk instead of one per 8), 2 x 2 outputs per thread.  Each output is the
+// same sequential fp32 FMA chain over k as in gemm_kernel.
+constexpr int SBM = 32, SBN = 32, SKC = 64, STHREADS = 256;
+
+__global__ void __launch_bounds__(STHREADS, 2) gemm_small_kernel(const GemmArgs g) {
+  __shared__ float As[SKC][SBM + 1];   // As[k][m]
+  __shared__ float Bs[SKC][SBN + 1];   // Bs[k][n]
+  const int64_t bz = blockIdx.z;
+  const float *A = g.A + bz * g.sA;
+  const float *B = g.B + bz * g.sB;
+  float *C = g.C + bz * g.sC;
+  const int64_t m0 = (int64_t)blockIdx.y * SBM, n0 = (int64_t)blockIdx.x * SBN;
+  if (g.lower && n0 > m0 + SBM - 1) return;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  constexpr int PER = SBM * SKC / STHREADS;   // 8 elements of each operand per thread and chunk
+  float ra[PER], rb[PER];
+  auto load = [&](int64_t k0) {
+#pragma unroll
+    for (int r = 0; r < PER; r++) {
+      const int e = tid + r * STHREADS;
+      int mm, kk, nn, kb;
+      if (g.ta) { kk = e / SBM; mm = e % SBM; } else { mm = e / SKC; kk = e % SKC; }
+      if (g.tb) { nn = e / SKC; kb = e % SKC; } else { kb = e / SBN; nn = e % SBN; }
+      const int64_t gm = m0 + mm, gka = k0 + kk, gn = n0 + nn, gkb = k0 + kb;
+      ra[r] = (gm < g.M && gka < g.K) ? (g.ta ? A[gka * g.lda + gm] : A[gm * g.lda + gka]) : 0.0f;
+      rb[r] = (gn < g.N && gkb < g.K) ? (g.tb ? B[gn * g.ldb + gkb] : B[gkb * g.ldb + gn]) : 0.0f;
+    }
+  };
+  auto store = [&]() {
+#pragma unroll
+    for (int r = 0; r < PER; r++) {
+      const int e = tid + r * STHREADS;
+      int mm, kk, nn, kb;
+      if (g.ta) { kk = e / SBM; mm = e % SBM; } else { mm = e / SKC; kk = e % SKC; }
+      if (g.tb) { nn = e / SKC; kb = e % SKC; } else { kb = e / SBN; nn = e % SBN; }
+      As[kk][mm] = ra[r];
+      Bs[kb][nn] = rb[r];
+    }
+  };
+  float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+  const int64_t nk = (g.K + SKC - 1) / SKC;
+  load(0);
+  store();
+  __syncthreads();
+  for (int64_t t = 0; t < nk; t++) {
+    if (t + 1 < nk) load((t + 1) * SKC);
+#pragma unroll 16
+    for (int kk = 0; kk < SKC; kk++) {
+      const float a0 = As[kk][ty], a1 = As[kk][ty + 16];
+      const float b0 = Bs[kk][tx], b1 = Bs[kk][tx + 16];
+      acc[0][0] = fmaf(a0, b0, acc[0][0]);
+      acc[0][1] = fmaf(a0, b1, acc[0][1]);
+      acc[1][0] = fmaf(a1, b0, acc[1][0]);
+      acc[1][1] = fmaf(a1, b1, acc[1][1]);
+    }
+    __syncthreads();
+    if (t + 1 < nk) {
+      store();
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int64_t gm = m0 + ty + 16 * i;
+    if (gm >= g.M) continue;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int64_t gn = n0 + tx + 16 * j;
+      if (gn >= g.N) continue;
+      float *cp = C + gm * g.ldc + gn;
+      const float v = g.alpha * acc[i][j];
+      *cp = g.beta == 0.0f ? v : fmaf(g.beta, *cp, v);
+    }
+  }
+}
+
 // --------------------------------------------------------------------------
 // Cholesky building blocks (lower, in place, row-major n x n, leading dim ld)
 constexpr int CB = 64;  // panel width
@@ -209,83 +287,290 @@ __global__ void __launch_bounds__(128) trsm_panel_kernel(float *A, int64_t ld, i
 }
 
 // Factor (optional) and invert one lower-triangular block of b <= 128 rows in
-// shared memory, one CTA of 1024 threads.
-//   do_factor: A's b x b block (leading dim ld) is SPD: Cholesky in place
-//   (right-looking, one column per step), L written back with zeros above the
-//   diagonal; info = 1 on a non-positive pivot.  Otherwise A already holds L.
-//   Then X = L^-1 by forward substitution, 8 lanes per column (warp shuffles,
-//   columns are independent so only warp-level syncs are needed), written to
-//   Linv (leading dim ldi; may alias A).
+// shared memory, one CTA of 256 threads, in 32-column panels.
+//   mode 1 (factor): A's b x b block (leading dim ld) is SPD: Cholesky in
+//   shared memory; info = 1 on a non-positive pivot (the pivot is then taken
+//   as 1).  Without it A already holds L.
+//   mode 2 (invert): X = L^-1 written to Linv (leading dim ldi; may alias A).
+//   mode 4 (keep): L written back to A, zeros above the diagonal.
+// The block is padded with the identity to bp = b rounded up to 32, which
+// leaves the b x b results unchanged and makes every diagonal block a full
+// 32 x 32 one, so the unrolled per-warp code below carries no bounds tests.
+// Per panel p (columns c0 .. c0+32): all threads factor the diagonal block,
+// one warp inverts it (lane c owns column c of the inverse); the rows below are
+// L21 = A21 L11^-T, a product with that inverse; the trailing lower triangle
+// gets the rank-32 update A22 -= L21 L21^T in 4 x 4 register tiles.  The
+// inverse's off-diagonal blocks then follow block-row by block-row:
+//   X_pq = -X_pp (sum_{k=q}^{p-1} L_pk X_kq).
 constexpr int PB = 128;
-__global__ void __launch_bounds__(1024) potrf_inv128_kernel(float *A, int64_t ld, int b, float *Linv, int64_t ldi,
-                                                            int *info, int mode) {
-  const int do_factor = mode & 1, do_invert = mode & 2;
-  extern __shared__ float sm[];
-  float *S = sm;                   // [PB][PB + 1]
-  float *X = sm + PB * (PB + 1);   // [PB][PB + 1]
-  const int tid = threadIdx.x;
-  for (int e = tid; e < b * b; e += blockDim.x) {
-    const int r = e / b, c = e % b;
-    S[r * (PB + 1) + c] = (c <= r) ? A[r * ld + c] : 0.0f;
+constexpr int LP = 32;                  // panel width
+constexpr int LTHREADS = 256;
+constexpr int LDS = PB + 1;             // shared-memory row pitch (floats)
+constexpr int LDT = PB - LP + 1;        // pitch of the T scratch (32 x 96)
+
+// One warp: X[c0.., c0..] = inverse of the 32 x 32 lower block of S at
+// (c0, c0), given rdiag = 1 / L[c0+lane][c0+lane] in each lane.  Lane c
+// computes column c by right-looking substitution: step k fixes
+// x_k = acc_k / L_kk and removes it from every later row, so each step is one
+// multiply followed by independent FMAs (entries above the diagonal come out
+// as zero).
+__device__ __forceinline__ void leaf_diag_invert(const float *S, float *X, int c0, int lane, float rdiag) {
+  float acc[LP], rd[LP];
+#pragma unroll
+  for (int i = 0; i < LP; i++) {
+    acc[i] = (i == lane) ? 1.0f : 0.0f;
+    rd[i] = __shfl_sync(0xffffffffu, rdiag, i);
+  }
+#pragma unroll
+  for (int k = 0; k < LP; k++) {
+    const float xk = acc[k] * rd[k];
+    acc[k] = xk;
+#pragma unroll
+    for (int i = k + 1; i < LP; i++) acc[i] = fmaf(-S[(c0 + i) * LDS + c0 + k], xk, acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < LP; i++) X[(c0 + i) * LDS + c0 + lane] = acc[i];
+}
+
+// All threads: Cholesky of the 32 x 32 block of S at (c0, c0) in place
+// (lower), then (warp 0) its inverse into X.  Right-looking on unscaled
+// columns: step j subtracts S[i][j] S[k][j] / S[j][j] from the trailing
+// triangle (one barrier per step, at most 4 elements per thread), and the
+// columns are scaled by 1 / sqrt(pivot) at the end.  A non-positive or
+// non-finite pivot sets info and is taken as 1.
+__device__ __forceinline__ void leaf_diag_factor(float *S, float *X, int c0, int tid, int *info) {
+  for (int j = 0; j < LP; j++) {
+    const float piv = S[(c0 + j) * LDS + c0 + j];
+    const bool bad = !(piv > 0.0f) || !isfinite(piv);
+    const float rp = bad ? 1.0f : __fdividef(1.0f, piv);
+    // element e = tid + 256 q of the rows below j: row j + 1 + e / 32, column e % 32
+#pragma unroll
+    for (int q = 0; q < LP * LP / LTHREADS; q++) {
+      const int e = tid + LTHREADS * q, i = j + 1 + e / LP, k = e % LP;
+      if (i < LP && k > j && k <= i)
+        S[(c0 + i) * LDS + c0 + k] = fmaf(-S[(c0 + i) * LDS + c0 + j] * rp, S[(c0 + k) * LDS + c0 + j],
+                                          S[(c0 + i) * LDS + c0 + k]);
+    }
+    __syncthreads();
+    if (tid == 0 && bad) {
+      if (info) atomicExch(info, 1);
+      S[(c0 + j) * LDS + c0 + j] = 1.0f;
+    }
   }
   __syncthreads();
+  // scale: L[i][j] = S[i][j] / sqrt(S[j][j]) (i > j), L[j][j] = sqrt(S[j][j])
+  float v[LP * LP / LTHREADS];
+#pragma unroll
+  for (int q = 0; q < LP * LP / LTHREADS; q++) {
+    const int e = tid + LTHREADS * q, i = e / LP, j = e % LP;
+    const float piv = S[(c0 + j) * LDS + c0 + j];
+    v[q] = (j == i) ? sqrtf(piv) : (j < i ? S[(c0 + i) * LDS + c0 + j] * rsqrtf(piv) : 0.0f);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < LP * LP / LTHREADS; q++) {
+    const int e = tid + LTHREADS * q, i = e / LP, j = e % LP;
+    S[(c0 + i) * LDS + c0 + j] = v[q];
+  }
+  __syncthreads();
+  if (tid < 32) leaf_diag_invert(S, X, c0, tid, 1.0f / S[(c0 + tid) * LDS + c0 + tid]);
+}
+
+__global__ void __launch_bounds__(LTHREADS, 1) potrf_inv128_kernel(float *A, int64_t ld, int b, float *Linv,
+                                                                   int64_t ldi, int *info, int mode) {
+  const int do_factor = mode & 1, do_invert = mode & 2;
+  extern __shared__ float sm[];
+  float *S = sm;                   // [PB][LDS]  L (lower; zeros above)
+  float *X = sm + PB * LDS;        // [PB][LDS]  L^-1
+  float *T = X + PB * LDS;         // [LP][LDT]  block-row scratch of the inverse
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NW = LTHREADS / 32;
+  constexpr int PER = PB * PB / LTHREADS;
+  const int bp = (b + LP - 1) / LP * LP;
+  {
+    float v[PER];
+#pragma unroll
+    for (int q = 0; q < PER; q++) {
+      const int e = tid + LTHREADS * q, r = e / PB, c = e % PB;
+      v[q] = (r < b && c <= r) ? A[r * ld + c] : 0.0f;
+    }
+#pragma unroll
+    for (int q = 0; q < PER; q++) {
+      const int e = tid + LTHREADS * q, r = e / PB, c = e % PB;
+      S[r * LDS + c] = (r >= b && r == c) ? 1.0f : v[q];
+      X[r * LDS + c] = 0.0f;
+    }
+  }
+  __syncthreads();
+  const int np = bp / LP;
   if (do_factor) {
-    for (int j = 0; j < b; j++) {
-      if (tid == 0) {
-        const float p = S[j * (PB + 1) + j];
-        if (!(p > 0.0f) || !isfinite(p)) {
-          atomicExch(info, 1);
-          S[j * (PB + 1) + j] = 1.0f;
-        } else {
-          S[j * (PB + 1) + j] = sqrtf(p);
+    for (int p = 0; p < np; p++) {
+      const int c0 = p * LP;
+      leaf_diag_factor(S, X, c0, tid, info);
+      __syncthreads();
+      const int r0 = c0 + LP, nr = bp - r0;
+      if (nr <= 0) break;
+      // L21 = A21 * X11^T (nr <= 96 rows x 32 columns): thread (rg, cg), rg < 24,
+      // cg < 8, owns rows r0 + rg + 24a and columns c0 + cg + 8c (a, c < 4);
+      // X11 is zero above its diagonal, so k runs over the whole panel
+      {
+        const int rg = tid >> 3, cg = tid & 7;
+        float acc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int c = 0; c < 4; c++) acc[a][c] = 0.0f;
+        if (rg < 24) {
+#pragma unroll 4
+          for (int k = 0; k < LP; k++) {
+            float av[4], xv[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+              const int i = r0 + rg + 24 * a;
+              av[a] = i < bp ? S[i * LDS + c0 + k] : 0.0f;
+              xv[a] = X[(c0 + cg + 8 * a) * LDS + c0 + k];
+            }
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+#pragma unroll
+              for (int c = 0; c < 4; c++) acc[a][c] = fmaf(av[a], xv[c], acc[a][c]);
+          }
+        }
+        __syncthreads();
+        if (rg < 24) {
+#pragma unroll
+          for (int a = 0; a < 4; a++) {
+            const int i = r0 + rg + 24 * a;
+            if (i < bp) {
+#pragma unroll
+              for (int c = 0; c < 4; c++) S[i * LDS + c0 + cg + 8 * c] = acc[a][c];
+            }
+          }
         }
       }
       __syncthreads();
-      const float djj = S[j * (PB + 1) + j];
-      for (int i = j + 1 + tid; i < b; i += blockDim.x) S[i * (PB + 1) + j] = S[i * (PB + 1) + j] / djj;
-      __syncthreads();
-      // rank-1 update of the trailing lower triangle: thread (ty, tx) of a
-      // 32 x 32 grid walks rows j+1+ty and columns j+1+tx in steps of 32
-      const int tx = tid & 31, ty = tid >> 5;
-      for (int r = j + 1 + ty; r < b; r += 32) {
-        const float srj = S[r * (PB + 1) + j];
-        for (int c = j + 1 + tx; c <= r; c += 32)
-          S[r * (PB + 1) + c] = fmaf(-srj, S[c * (PB + 1) + j], S[r * (PB + 1) + c]);
+      // A22 -= L21 L21^T on the lower triangle: warp tiles of 16 rows x 32
+      // columns, lane = 4 x 4 register tile (rows 4*(lane/8), cols 4*(lane%8))
+      const int wtr = nr / 16, wtc = nr / 32;
+      for (int wt = warp; wt < wtr * wtc; wt += NW) {
+        const int wr = wt / wtc, wc = wt % wtc;
+        if (wc * 32 > wr * 16 + 15) continue;   // entirely above the diagonal
+        const int i0 = r0 + wr * 16 + 4 * (lane >> 3), k0 = r0 + wc * 32 + 4 * (lane & 7);
+        float acc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int c = 0; c < 4; c++) acc[a][c] = 0.0f;
+#pragma unroll 4
+        for (int j = 0; j < LP; j++) {
+          float li[4], lk[4];
+#pragma unroll
+          for (int a = 0; a < 4; a++) {
+            li[a] = S[(i0 + a) * LDS + c0 + j];
+            lk[a] = S[(k0 + a) * LDS + c0 + j];
+          }
+#pragma unroll
+          for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) acc[a][c] = fmaf(li[a], lk[c], acc[a][c]);
+        }
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            const int i = i0 + a, k = k0 + c;
+            if (k <= i) S[i * LDS + k] -= acc[a][c];
+          }
       }
       __syncthreads();
     }
-    for (int e = tid; e < b * b; e += blockDim.x) {
-      const int r = e / b, c = e % b;
-      A[r * ld + c] = (c <= r) ? S[r * (PB + 1) + c] : 0.0f;
+    if (mode & 4) {
+#pragma unroll 8
+      for (int q = 0; q < PER; q++) {
+        const int e = tid + LTHREADS * q, r = e / PB, c = e % PB;
+        if (r < b && c < b) A[r * ld + c] = (c <= r) ? S[r * LDS + c] : 0.0f;
+      }
     }
+  } else if (do_invert) {
+    if (warp < np) {
+      const int c0 = warp * LP;
+      leaf_diag_invert(S, X, c0, lane, 1.0f / S[(c0 + lane) * LDS + c0 + lane]);
+    }
+    __syncthreads();
   }
   if (!do_invert) return;
-  // inverse: column c = tid / 8, sub-lane sl = tid % 8
-  const int c = tid >> 3, sl = tid & 7;
-  for (int i = 0; i < b; i++) {
-    float part = 0.0f;
-    if (c < b && i > c)
-      for (int j = c + sl; j < i; j += 8) part = fmaf(S[i * (PB + 1) + j], X[j * (PB + 1) + c], part);
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    part += __shfl_xor_sync(0xffffffffu, part, 4);
-    if (sl == 0 && c < b) X[i * (PB + 1) + c] = (i < c) ? 0.0f : ((i == c ? 1.0f : 0.0f) - part) / S[i * (PB + 1) + i];
-    __syncwarp();
+  // off-diagonal blocks of the inverse, block-row p = 1 .. np-1; thread
+  // (rg, cg), rg < 8, cg < 8p, owns rows rg + 8a and columns cg + 8p*c
+  for (int p = 1; p < np; p++) {
+    const int c0 = p * LP, cs = 8 * p;
+    const int rg = tid / cs, cg = tid % cs;
+    const bool act = rg < 8;
+    float acc[4][4];
+    // T[i][c] = sum_{k<c0} L[c0+i][k] X[k][c]   (X[k][c] = 0 for k < c)
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) acc[a][c] = 0.0f;
+    if (act) {
+#pragma unroll 4
+      for (int k = cg; k < c0; k++) {
+        float lv[4], xv[4];
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+          lv[a] = S[(c0 + rg + 8 * a) * LDS + k];
+          xv[a] = X[k * LDS + cg + cs * a];
+        }
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int c = 0; c < 4; c++) acc[a][c] = fmaf(lv[a], xv[c], acc[a][c]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) T[(rg + 8 * a) * LDT + cg + cs * c] = acc[a][c];
+    }
+    __syncthreads();
+    // X[c0+i][c] = -sum_m X[c0+i][c0+m] T[m][c]   (X_pp is lower)
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) acc[a][c] = 0.0f;
+    if (act) {
+#pragma unroll 4
+      for (int m = 0; m < LP; m++) {
+        float xv[4], tv[4];
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+          xv[a] = X[(c0 + rg + 8 * a) * LDS + c0 + m];
+          tv[a] = T[m * LDT + cg + cs * a];
+        }
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int c = 0; c < 4; c++) acc[a][c] = fmaf(xv[a], tv[c], acc[a][c]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) X[(c0 + rg + 8 * a) * LDS + cg + cs * c] = -acc[a][c];
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  for (int e = tid; e < b * b; e += blockDim.x) {
-    const int r = e / b, cc = e % b;
-    Linv[r * ldi + cc] = (cc <= r) ? X[r * (PB + 1) + cc] : 0.0f;
+#pragma unroll 8
+  for (int q = 0; q < PER; q++) {
+    const int e = tid + LTHREADS * q, r = e / PB, c = e % PB;
+    if (r < b && c < b) Linv[r * ldi + c] = (c <= r) ? X[r * LDS + c] : 0.0f;
   }
 }
 
-// mode bits: 1 = factor A in place, 2 = write L^-1 to Linv
+// mode bits: 1 = factor A, 2 = write L^-1 to Linv, 4 = write L back to A
 static int potrf_inv128(float *A, int64_t ld, int b, float *Linv, int64_t ldi, int *info, int mode,
                         cudaStream_t s) {
-  const int smem = (int)(2 * PB * (PB + 1) * sizeof(float));
+  const int smem = (int)((2 * PB * LDS + LP * LDT) * sizeof(float));
   if (cudaFuncSetAttribute(potrf_inv128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return HIF4X_ERR_LAUNCH;
-  potrf_inv128_kernel<<<1, 1024, smem, s>>>(A, ld, b, Linv, ldi, info, mode);
+  potrf_inv128_kernel<<<1, LTHREADS, smem, s>>>(A, ld, b, Linv, ldi, info, mode);
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
 }
@@ -296,6 +581,15 @@ __global__ void reverse_square_kernel(const float *in, float *out, int64_t n, in
   if (e >= nn_total) return;
   const int64_t b = e / (n * n), r = (e / n) % n, c = e % n;
   out[e] = in[b * n * n + (n - 1 - r) * n + (n - 1 - c)];
+}
+
+// J X J in place for an n x n row-major X: element e <-> element n*n - 1 - e
+__global__ void reverse_flat_kernel(float *X, int64_t nn) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nn / 2) return;
+  const float a = X[e];
+  X[e] = X[nn - 1 - e];
+  X[nn - 1 - e] = a;
 }
 
 // Add the reference's damping d = max(mean(diag), 1e-30) * damp to the diagonal
@@ -556,8 +850,10 @@ static int gemm_simt_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float a
                         int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream);
 
-// Products of at least this many multiply-adds go to the tensor cores.
-static const int64_t kTcMinMacs = int64_t(1) << 26;
+// Products of at least this many multiply-adds go to the tensor cores;
+// smaller ones (per batch element) take the 32 x 32-tile SIMT kernel.
+static const int64_t kTcMinMacs = int64_t(1) << 27;
+static const int64_t kSmallMaxMacs = int64_t(1) << 27;
 
 static int gemm_dispatch(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
                          int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
@@ -606,6 +902,13 @@ static int gemm_simt_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float a
   if (M == 0 || N == 0 || batch == 0) return HIF4X_OK;
   if (!A || !B || !C || batch > 65535) return HIF4X_ERR_ARG;
   GemmArgs g{ta, tb, M, N, K, alpha, beta, A, lda, strideA, B, ldb, strideB, C, ldc, strideC, lower};
+  if (M * N * K < kSmallMaxMacs) {
+    dim3 grid(nblk(N, SBN), nblk(M, SBM), (unsigned)batch);
+    if (grid.y > 65535) return HIF4X_ERR_ARG;
+    gemm_small_kernel<<<grid, STHREADS, 0, (cudaStream_t)stream>>>(g);
+    HIF4X_CHECK_LAUNCH();
+    return HIF4X_OK;
+  }
   dim3 grid(nblk(N, GBN), nblk(M, GBM), (unsigned)batch);
   if (grid.y > 65535) return HIF4X_ERR_ARG;
   gemm_kernel<<<grid, GTHREADS, 0, (cudaStream_t)stream>>>(g);
@@ -636,43 +939,38 @@ static int potrf_lower(float *A, int64_t n, int *info_dev, cudaStream_t s) {
   return potrf_lower_ld(A, n, n, info_dev, s);
 }
 
-// dst (rows x cols, ldd) = src (lds); zero_upper clears dst[i][j] for j > i.
-__global__ void copy2d_kernel(const float *src, int64_t lds, float *dst, int64_t ldd, int64_t rows, int64_t cols,
-                              int zero_upper) {
-  const int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  if (e >= rows * cols) return;
-  const int64_t r = e / cols, c = e % cols;
-  dst[r * ldd + c] = (zero_upper && c > r) ? 0.0f : src[r * lds + c];
-}
-
 static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_t s);
 
-// Recursive lower Cholesky in place of the n x n block at A (leading dim ld):
-//   L11 = chol(A11);  L21 = A21 L11^-T;  L22 = chol(A22 - L21 L21^T).
-// L21 is one GEMM against L11's inverse and the update one large-K GEMM over
-// the lower-triangle tiles, so almost all flops run as big tensor-core GEMMs;
-// leaves of <= 128 rows are factored in shared memory by one CTA.  The upper
-// triangle is left stale (cleared by the caller).
-// Split n1 = n/2 rounded down to a multiple of 128 (at least 128), so
-// n1 <= n/2 and the workspace n1*n1 + max(n2*n1, n1*n1/4) is at most n*n/2
-// floats (the recursive calls reuse it after this level is done with it).
-static int potrf_rec(float *A, int64_t n, int64_t ld, int *info_dev, float *work, cudaStream_t s) {
-  if (n <= PB) return potrf_inv128(A, ld, (int)n, nullptr, 0, info_dev, 1, s);
+// Recursive lower Cholesky that carries the inverse along, for the n x n
+// block at A (leading dim ld) and the block at Inv (leading dim ldi):
+//   L11 = chol(A11), L11^-1            recursively
+//   L21 = A21 L11^-T                   one GEMM, into Inv21 (still free)
+//   A22 -= L21 L21^T                   large-K GEMM over the lower tiles
+//   L22 = chol(A22), L22^-1            recursively
+//   Inv21 = -L22^-1 (L21 L11^-1)       two GEMMs (T = L21 L11^-1 in work)
+// so L^-1 = [[L11^-1, 0], [Inv21, L22^-1]] is built without a separate
+// triangular inverse, and all flops but the 128-row leaves (factor and
+// inverse fused in shared memory by one CTA) run as GEMMs.  A keeps Schur
+// complements, not the factor.  Inv must be zero above the diagonal on entry.
+// Split n1 = n/2 rounded down to a multiple of 128 (at least 128); work holds
+// T (n2 x n1 <= n*n/4 floats), used only after both recursive calls return.
+static int potrf_inv_rec(float *A, int64_t n, int64_t ld, float *Inv, int64_t ldi, int *info_dev, float *work,
+                         cudaStream_t s) {
+  if (n <= PB) return potrf_inv128(A, ld, (int)n, Inv, ldi, info_dev, 3, s);
   const int64_t n1 = std::max<int64_t>(PB, (n / 2 / PB) * PB), n2 = n - n1;
-  float *A11 = A, *A21 = A + n1 * ld, *A22 = A + n1 * ld + n1;
-  int st = potrf_rec(A11, n1, ld, info_dev, work, s);
+  float *A21 = A + n1 * ld, *A22 = A + n1 * ld + n1;
+  float *I11 = Inv, *I21 = Inv + n1 * ldi, *I22 = Inv + n1 * ldi + n1;
+  int st = potrf_inv_rec(A, n1, ld, I11, ldi, info_dev, work, s);
   if (st) return st;
-  float *Linv = work;             // n1 x n1
-  float *T = work + n1 * n1;      // n2 x n1, and trtri's n1*n1/4 scratch before that
-  copy2d_kernel<<<nblk(n1 * n1, 256), 256, 0, s>>>(A11, ld, Linv, n1, n1, n1, 1);
-  st = trtri_lower(Linv, n1, n1, T, s);
+  st = gemm_dispatch(0, 1, n2, n1, n1, 1.0f, A21, ld, 0, I11, ldi, 0, 0.0f, I21, ldi, 0, 1, 0, s);
   if (st) return st;
-  st = gemm_dispatch(0, 1, n2, n1, n1, 1.0f, A21, ld, 0, Linv, n1, 0, 0.0f, T, n1, 0, 1, 0, s);   // T = A21 L11^-T
+  st = gemm_dispatch(0, 1, n2, n2, n1, -1.0f, I21, ldi, 0, I21, ldi, 0, 1.0f, A22, ld, 0, 1, 1, s);
   if (st) return st;
-  copy2d_kernel<<<nblk(n2 * n1, 256), 256, 0, s>>>(T, n1, A21, ld, n2, n1, 0);
-  st = gemm_dispatch(0, 1, n2, n2, n1, -1.0f, A21, ld, 0, A21, ld, 0, 1.0f, A22, ld, 0, 1, 1, s);
+  st = potrf_inv_rec(A22, n2, ld, I22, ldi, info_dev, work, s);
   if (st) return st;
-  return potrf_rec(A22, n2, ld, info_dev, work, s);
+  st = gemm_dispatch(0, 0, n2, n1, n1, 1.0f, I21, ldi, 0, I11, ldi, 0, 0.0f, work, n1, 0, 1, 0, s);
+  if (st) return st;
+  return gemm_dispatch(0, 0, n2, n1, n2, -1.0f, I22, ldi, 0, work, n1, 0, 0.0f, I21, ldi, 0, 1, 0, s);
 }
 
 // In-place inverse of a lower-triangular n x n block at A (leading dim ld):
@@ -698,24 +996,17 @@ extern "C" int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, fl
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t nn = n * n;
   if (cudaMemsetAsync(info_dev, 0, sizeof(int), s) != cudaSuccess) return HIF4X_ERR_LAUNCH;
-  // work: [nn] reversed matrix per batch element + [nn] scratch for trtri
+  // work: [nn] reversed damped matrix (overwritten by Schur complements) +
+  // [nn/4] GEMM scratch; L^-1 is built in U itself and reversed in place.
   for (int64_t b = 0; b < batch; b++) {
     float *P = work;
-    float *scratch = work + nn;
+    float *Inv = U + b * nn;
     reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(H + b * nn, P, n, nn);
     damp_diag_kernel<<<1, 1024, 0, s>>>(P, n, damp);
-    int st;
-    if (n <= PB) {
-      st = potrf_inv128(P, n, (int)n, P, n, info_dev, 3, s);   // L^-1 in place
-      if (st) return st;
-    } else {
-      st = potrf_rec(P, n, n, info_dev, scratch, s);
-      if (st) return st;
-      zero_upper_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, n, nn);
-      st = trtri_lower(P, n, n, scratch, s);
-      if (st) return st;
-    }
-    reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(P, U + b * nn, n, nn);
+    if (cudaMemsetAsync(Inv, 0, (size_t)nn * sizeof(float), s) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+    const int st = potrf_inv_rec(P, n, n, Inv, n, info_dev, work + nn, s);
+    if (st) return st;
+    reverse_flat_kernel<<<nblk((nn + 1) / 2, 256), 256, 0, s>>>(Inv, nn);
   }
   HIF4X_CHECK_LAUNCH();
   int info = 0;

@@ -190,10 +190,11 @@ int hif4x_device_status(void *stream);
 
 /* _upper_cholesky_inv (example/solution/solution.py:287-300): U upper with
  * U^T U = (H + damp * max(mean(diag H), 1e-30) I)^-1, for `batch` n x n
- * matrices.  Computed as one Cholesky of the index-reversed matrix and one
- * triangular inverse (U = J L^-1 J with J H J = L L^T).  Synchronises the
- * stream; returns HIF4X_NOT_PD (U undefined) where the reference's torch
- * Cholesky would raise.  work: 2*n*n floats; info_dev: one device int. */
+ * matrices.  Computed as U = J L^-1 J with J H J = L L^T: one recursive
+ * Cholesky of the index-reversed matrix that builds L^-1 as it goes.
+ * Synchronises the stream; returns HIF4X_NOT_PD (U undefined) where the
+ * reference's torch Cholesky would raise.  work: 2*n*n floats (1.25*n*n
+ * used); info_dev: one device int. */
 int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
                          int *info_dev, void *stream);
 

@@ -30,6 +30,17 @@ def test_gemm_vs_torch(ta, tb, M, N, K):
     assert float((got.double() - ref).abs().max()) <= tol
 
 
+@pytest.mark.parametrize("M,N,K", [(96, 200, 33), (520, 520, 520)])
+def test_gemm_exact_path_vs_torch(M, N, K):
+    """The SIMT path kept for differenced products: 32 x 32 tiles below 2^27
+    multiply-adds, 128 x 128 tiles above."""
+    A, B = rnd(M, K, seed=11), rnd(N, K, seed=12)
+    ref = A.double() @ B.double().T
+    got = la.gemm(A, B, tb=True, exact=True)
+    tol = 2e-6 * np.sqrt(K) * float(ref.abs().max()) + 1e-6
+    assert float((got.double() - ref).abs().max()) <= tol
+
+
 def test_gemm_accumulate_strided_batched():
     A = rnd(3, 40, 50, seed=3)
     B = rnd(50, 60, seed=4)
