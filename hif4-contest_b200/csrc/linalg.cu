@@ -627,11 +627,15 @@ __global__ void zero_upper_kernel(float *A, int64_t n, int64_t total) {
 // for j > i inside the block (example/solution/solution.py:316-326).
 constexpr int GQ_THREADS = 128;
 constexpr int GQ_BLK = 128;
-constexpr int GQW_WARPS = 8;   // rows per CTA in the warp-per-row kernel
+constexpr int GQW_WARPS = 8;   // warps per CTA in the warp-per-rows kernel
 
-// Warp-per-row form: lane l owns block columns l, l+32, l+64, l+96 in
-// registers; column i's owner quantizes it and broadcasts the scaled error,
-// every lane updates its own later columns.  U's block sits in shared memory.
+// Warp-per-rows form: each warp owns GQW_ROWS rows; lane l holds block
+// columns l, l+32, l+64, l+96 of each of them in registers.  Column i's owner
+// lane quantizes it for all of the warp's rows (independent chains, so their
+// latencies overlap), broadcasts the scaled errors, and every lane updates its
+// own later columns; one shared-memory read of U's row serves all the rows.
+// U's block sits in shared memory.
+template <int GQW_ROWS>
 __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_warp_kernel(float *W, const float *unit, const float *U,
                                                                          float *Q, float *E, int64_t R, int64_t C,
                                                                          int64_t i1, int nb, int64_t bstride_rows,
@@ -646,47 +650,67 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_warp_kernel(float *
   for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t r = (int64_t)blockIdx.x * GQW_WARPS + (threadIdx.x >> 5);
-  if (r >= R) return;
-  float w[4], u[4], q[4], err[4];
+  const int64_t r0 = ((int64_t)blockIdx.x * GQW_WARPS + (threadIdx.x >> 5)) * GQW_ROWS;
+  if (r0 >= R) return;
+  float w[GQW_ROWS][4], u[GQW_ROWS][4], q[GQW_ROWS][4], err[GQW_ROWS][4];
 #pragma unroll
-  for (int k = 0; k < 4; k++) {
-    const int c = lane + 32 * k;
-    w[k] = c < nb ? W[r * C + i1 + c] : 0.0f;
-    u[k] = c < nb ? unit[r * C + i1 + c] : 1.0f;
-    q[k] = 0.0f;
-    err[k] = 0.0f;
+  for (int rr = 0; rr < GQW_ROWS; rr++) {
+    const int64_t r = r0 + rr;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int c = lane + 32 * k;
+      const bool in = r < R && c < nb;
+      w[rr][k] = in ? W[r * C + i1 + c] : 0.0f;
+      u[rr][k] = in ? unit[r * C + i1 + c] : 1.0f;
+      q[rr][k] = 0.0f;
+      err[rr][k] = 0.0f;
+    }
   }
 #pragma unroll
   for (int k = 0; k < 4; k++) {
     for (int ii = 0; ii < 32; ii++) {
       const int i = 32 * k + ii;
       if (i >= nb) break;
-      float ei = 0.0f;
-      if (lane == ii) {
-        const float wi = w[k], ui = u[k];
-        float m = rintf(__fmul_rn(__fdiv_rn(fabsf(wi), ui), 4.0f));
-        m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
-        const float qi = __fmul_rn(__fmul_rn(wi >= 0.0f ? 1.0f : -1.0f, m), ui);
-        q[k] = qi;
-        ei = __fdiv_rn(__fsub_rn(wi, qi), fmaxf(Hs[i * nb + i], 1e-30f));
-        err[k] = ei;
+      float ei[GQW_ROWS];
+      const float hii = fmaxf(Hs[i * nb + i], 1e-30f);
+#pragma unroll
+      for (int rr = 0; rr < GQW_ROWS; rr++) {
+        ei[rr] = 0.0f;
+        if (lane == ii) {
+          const float wi = w[rr][k], ui = u[rr][k];
+          float m = rintf(__fmul_rn(__fdiv_rn(fabsf(wi), ui), 4.0f));
+          m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
+          const float qi = __fmul_rn(__fmul_rn(wi >= 0.0f ? 1.0f : -1.0f, m), ui);
+          q[rr][k] = qi;
+          ei[rr] = __fdiv_rn(__fsub_rn(wi, qi), hii);
+          err[rr][k] = ei[rr];
+        }
       }
-      ei = __shfl_sync(0xffffffffu, ei, ii);
+#pragma unroll
+      for (int rr = 0; rr < GQW_ROWS; rr++) ei[rr] = __shfl_sync(0xffffffffu, ei[rr], ii);
       const float *hrow = Hs + i * nb;
 #pragma unroll
       for (int kk = 0; kk < 4; kk++) {
         const int c = lane + 32 * kk;
-        if (kk >= k && c > i && c < nb) w[kk] = fmaf(-ei, hrow[c], w[kk]);
+        if (kk >= k && c > i && c < nb) {
+          const float h = hrow[c];
+#pragma unroll
+          for (int rr = 0; rr < GQW_ROWS; rr++) w[rr][kk] = fmaf(-ei[rr], h, w[rr][kk]);
+        }
       }
     }
   }
 #pragma unroll
-  for (int k = 0; k < 4; k++) {
-    const int c = lane + 32 * k;
-    if (c < nb) {
-      Q[r * C + i1 + c] = q[k];
-      E[r * GQ_BLK + c] = err[k];
+  for (int rr = 0; rr < GQW_ROWS; rr++) {
+    const int64_t r = r0 + rr;
+    if (r >= R) break;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int c = lane + 32 * k;
+      if (c < nb) {
+        Q[r * C + i1 + c] = q[rr][k];
+        E[r * GQ_BLK + c] = err[rr][k];
+      }
     }
   }
 }
@@ -1028,13 +1052,21 @@ extern "C" int hif4x_gptq(const float *X, const float *unit, const float *U, int
   if (cudaMemcpyAsync(W, X, sizeof(float) * batch * R * C, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return HIF4X_ERR_LAUNCH;
   const size_t smem = sizeof(float) * GQ_BLK * GQ_BLK;
-  if (cudaFuncSetAttribute(gptq_block_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess)
+  // 4 rows per warp when that still gives two waves of CTAs, else 1
+  const bool four = (int64_t)nblk(R, GQW_WARPS * 4) * batch >= 2 * 148;
+  if (cudaFuncSetAttribute(gptq_block_warp_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(gptq_block_warp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
     return HIF4X_ERR_LAUNCH;
   for (int64_t i1 = 0; i1 < C; i1 += GQ_BLK) {
     const int nb = (int)std::min<int64_t>(GQ_BLK, C - i1);
-    dim3 grid(nblk(R, GQW_WARPS), (unsigned)batch);
-    gptq_block_warp_kernel<<<grid, GQW_WARPS * 32, smem, s>>>(W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
+    if (four)
+      gptq_block_warp_kernel<4><<<dim3(nblk(R, GQW_WARPS * 4), (unsigned)batch), GQW_WARPS * 32, smem, s>>>(
+          W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
+    else
+      gptq_block_warp_kernel<1><<<dim3(nblk(R, GQW_WARPS), (unsigned)batch), GQW_WARPS * 32, smem, s>>>(
+          W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
     HIF4X_CHECK_LAUNCH();
     const int64_t i2 = i1 + nb;
     if (i2 < C) {

@@ -92,6 +92,18 @@ def _randperm(n: int, k: int, dev) -> torch.Tensor:
     return torch.randperm(n)[:min(n, k)].to(dev)
 
 
+def _resid(x: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """x @ a^T - x @ b^T computed as x @ (a - b)^T: the product of the small
+    difference runs on the tensor cores with its error relative to the
+    residual itself, not to the two cancelling products."""
+    return la.gemm(x, la.sub(a, b), tb=True)
+
+
+def _resid_mse(x: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> float:
+    """mse(x @ a^T, x @ b^T), the reference's hold-out and search losses."""
+    return la.mse(_resid(x, a, b))
+
+
 def _refine_weight_values(w_final, q_used, weight_params: Dict5, calib_sm, mode):
     """_refine_weight_values (solution.py:666-723)."""
     if len(calib_sm) < 2:
@@ -115,13 +127,12 @@ def _refine_weight_values(w_final, q_used, weight_params: Dict5, calib_sm, mode)
     if rows == 0 or xh.shape[0] == 0:
         return weight_params, q_used
     A = la.gemm(la.sub(q_used, w_final), Gxx)          # (q - w_final) @ Gxx
-    ref_h = la.gemm(xh, w_final, tb=True, exact=True)
-    hold0 = la.mse(la.gemm(xh, q_used, tb=True, exact=True), ref_h)
+    hold0 = _resid_mse(xh, q_used, w_final)
     if not (0.0 < hold0 < float("inf")):
         return weight_params, q_used
     la.refine_rows(A, v4, d, Gxx, REFINE_W_SWEEPS * REFINE_ACT_ROUNDS)
     wn = la.mul(v4, d)
-    hold1 = la.mse(la.gemm(xh, wn, tb=True, exact=True), ref_h)
+    hold1 = _resid_mse(xh, wn, w_final)
     if hold1 < hold0:
         return codec.values_to_params(wn, weight_params), wn
     return weight_params, q_used
@@ -154,12 +165,11 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     logm = la.smooth_logm(abs_sum, n_tok)
     rows = _randperm(R, 256, dev)                              # solution.py:858
     w_rows = la.gather_rows(w, rows)
-    a_wr = la.gemm(a_big, w_rows, tb=True, exact=True)
     best_alpha, best_loss = 0.0, None
     for alpha in ALPHA_GRID:
         s = la.exp_scale(logm, alpha)
         wq = la.scale_cols(_encode_fast(w_rows, s)["deq"], s, L.SMOOTH_MUL)
-        loss = la.mse(la.gemm(a_big, wq, tb=True, exact=True), a_wr)
+        loss = _resid_mse(a_big, wq, w_rows)
         if best_loss is None or loss < best_loss:
             best_loss, best_alpha = loss, alpha
     s = la.exp_scale(logm, best_alpha)
@@ -191,7 +201,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
             pp = _encode_fast(w_rsub)
             qq = la.gptq(w_rsub, pp["unit"], U)
             xt = tf(xh_sub, md)
-            cand.append(la.mse(la.gemm(xt, qq, tb=True, exact=True), la.gemm(xt, w_rsub, tb=True, exact=True)))
+            cand.append(_resid_mse(xt, qq, w_rsub))
         mode = min(range(2), key=lambda i: (cand[i], i)) if not all(math.isnan(c) for c in cand) else 0
         if mode == 1 and spaces[1] is None:
             mode = 0
@@ -201,20 +211,22 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
 
     ph.mark("transform_choice")
     w_final = tf(w_s, mode)
-    ref_shared = None
+    res_q = None   # xh_pick @ (q_used - w_final)^T, the hold-out residual of the weight choice
     # ---- searched encode + hold-out-guarded GPTQ (solution.py:921-934)
     weight_params, q_used, unit = _search(w_final)
     gptq_w = False
     if xh_pick is not None and Uw is not None:
         q_g = la.gptq(w_final, unit, Uw)
-        ref = la.gemm(xh_pick, w_final, tb=True, exact=True)
-        ref_shared = ref
-        mse_r = la.mse(la.gemm(xh_pick, q_used, tb=True, exact=True), ref)
-        mse_g = la.mse(la.gemm(xh_pick, q_g, tb=True, exact=True), ref)
+        res_r = _resid(xh_pick, q_used, w_final)
+        res_g = _resid(xh_pick, q_g, w_final)
+        mse_r, mse_g = la.mse(res_r), la.mse(res_g)
+        res_q = res_r
         if mse_g < mse_r:
             weight_params = codec.values_to_params(q_g, weight_params)
             q_used = q_g
             gptq_w = True
+            res_q = res_g
+        del res_r, res_g
     del Uw
     ph.mark("weight_encode_gptq")
 
@@ -234,9 +246,11 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
                 xg = la.scatter_cols(la.gptq(la.gather_cols(xh_pick, order), la.gather_cols(unit_x, order), Ua), order)
             else:
                 xg = la.gptq(xh_pick, unit_x, Ua)
-            ref2 = ref_shared if ref_shared is not None else la.gemm(xh_pick, w_final, tb=True, exact=True)
-            mse_ar = la.mse(la.gemm(xr, q_used, tb=True, exact=True), ref2)
-            mse_ag = la.mse(la.gemm(xg, q_used, tb=True, exact=True), ref2)
+            # x' @ q^T - xh @ w^T = (x' - xh) @ q^T + xh @ (q - w)^T
+            if res_q is None:
+                res_q = _resid(xh_pick, q_used, w_final)
+            mse_ar = la.mse(la.gemm(la.sub(xr, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone()))
+            mse_ag = la.mse(la.gemm(la.sub(xg, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone()))
             if mse_ag < mse_ar:
                 u_act = Ua
                 gptq_act = 1
