@@ -381,11 +381,15 @@ def run_layer(args, rank, ws, local_rank):
             step(device_resident)
         torch.cuda.synchronize(dev)
         barrier()
-        t0 = time.perf_counter()
+        # CUDA events on the stream every kernel of the step is launched on
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
         for _ in range(args.steps):
             step(device_resident)
+        e1.record()
         torch.cuda.synchronize(dev)
-        dt = (time.perf_counter() - t0) / max(args.steps, 1)
+        dt = e0.elapsed_time(e1) / 1e3 / max(args.steps, 1)
         if dist is not None:
             t = torch.tensor([dt], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -416,7 +420,96 @@ def run_layer(args, rank, ws, local_rank):
         "weight_gelem_per_s": elems / dt / 1e9, "gather_s": gather_s,
         "e2e": {"value": len(jobs) / dt_api, "unit": "matrices/s", "ms_per_step": dt_api * 1e3,
                 "note": "through the six-function API: CPU tensors in, CPU dict5 and CPU states out"},
-        "timing_note": "host wall clock around device-synchronised steps, max over ranks",
+        "timing_note": "CUDA events on the launching stream around the timed steps, max over ranks",
+    }), flush=True)
+
+
+def run_attention(args, rank, ws, local_rank):
+    """Attention workload: 8 independent batch items of Q (4096, 32*128) and
+    K, V (4096, 8*128) bf16 NVFP4 (GQA 4:1, K with RoPE-paired channels and
+    4 outlier pairs x15 per head, V N(0,1)).  Per item: the attention
+    calibration (rotation and Q/K GPTQ decisions from one 1024-token Hessian
+    sample plus the 4096-token hold-out) and the dynamic conversion of its
+    Q, K and V.  Items are dealt round-robin to the ranks (fixed total work:
+    strong scaling, no collective on the data path).  value = Q/K/V elements
+    converted per second over all ranks; quality = relative error of
+    softmax(QK^T/sqrt(128))V from the converted tensors against bf16."""
+    import torch
+
+    from hif4x import attention, codec, synth
+    from hif4x import linalg as la
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+    B, T, T_cal, qh, kvh, dh = 8, 4096, 1024, 32, 8, 128
+    mine = [b for b in range(B) if b % ws == rank]
+
+    def sample(seed, Tn):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        q = torch.randn(Tn, qh * dh, generator=g, device=dev).to(torch.bfloat16)
+        k = synth.kv_rope(seed + 1, Tn, kvh, dh, device=dev)
+        v = torch.randn(Tn, kvh * dh, generator=g, device=dev).to(torch.bfloat16)
+        return {"q": q, "k": k, "v": v}
+
+    raw = {b: (sample(1000 + 10 * b, T_cal), sample(1005 + 10 * b, T)) for b in mine}
+    nv = {b: [{r: list(synth.reference_form(*synth.quantize_nvfp4(x[r]))) for r in "qkv"} for x in raw[b]]
+          for b in mine}
+    torch.cuda.synchronize(dev)
+
+    outs = {}
+
+    def step():
+        for b in mine:
+            calib = nv[b]
+            st = attention.calibrate(calib, qh, kvh, dh)
+            test = calib[-1]
+            pq = attention.dynamic_qk(test["q"][0], test["q"][1], st["q_state"], qh, dh, return_device=True)
+            pk = attention.dynamic_qk(test["k"][0], test["k"][1], st["k_state"], kvh, dh, return_device=True)
+            pv = attention.dynamic_v(test["v"][0], test["v"][1], st["v_state"], kvh, dh, return_device=True)
+            outs[b] = (pq, pk, pv)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    dt = e0.elapsed_time(e1) / 1e3 / max(args.steps, 1)
+    # quality on this rank's first item: converted vs bf16 attention output
+    rel = float("nan")
+    if mine:
+        b = mine[0]
+        x = raw[b][1]
+        pq, pk, pv = outs[b]
+        ref = attention.attention_out(x["q"].float(), x["k"].float(), x["v"].float(), qh, kvh, dh)
+        got = attention.attention_out(codec.decode(pq), codec.decode(pk), codec.decode(pv), qh, kvh, dh)
+        rel = la.mse(got, ref) / max(la.mse(ref), 1e-30)
+    if dist is not None:
+        t = torch.tensor([dt], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t[0])
+    if rank != 0:
+        return
+    elems = B * T * (qh + 2 * kvh) * dh
+    print(json.dumps({
+        "metric": "attention Q/K/V NVFP4->HiF4 Gelem/s (calibration + dynamic q/k/v per batch item)",
+        "value": elems / dt / 1e9, "unit": "Gelem/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"attention config: {B} items of Q ({T}, {qh}x{dh}), K/V ({T}, {kvh}x{dh}) "
+                               f"bf16 NVFP4, GQA {qh // kvh}:1, K RoPE-paired with 4 outlier pairs x15; "
+                               f"calibration from 1 x {T_cal}-token sample + {T}-token hold-out",
+                   "parallelism": f"batch items round-robin over {ws} GPU(s)"},
+        "quality": {"rel_err_softmax_qkv": rel, "item": mine[0] if mine else None},
+        "timing_note": "CUDA events on the launching stream, max over ranks",
     }), flush=True)
 
 
@@ -428,7 +521,7 @@ def main():
     ap.add_argument("--impl", default="hif4x", choices=["hif4x", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
-    ap.add_argument("--workload", default="codec", choices=["codec", "layer"])
+    ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention"])
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "codec":
@@ -441,6 +534,8 @@ def main():
     try:
         if args.workload == "layer":
             run_layer(args, rank, ws, local_rank)
+        elif args.workload == "attention":
+            run_attention(args, rank, ws, local_rank)
         else:
             run_gpu(args, rank, ws, local_rank)
     finally:
