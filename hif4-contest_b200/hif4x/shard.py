@@ -36,12 +36,13 @@ class MatrixJob:
 
 
 def matrix_cost(N: int, C: int, T_cal: int) -> float:
-    """Seconds to calibrate one N x C matrix (plus one dynamic call) on one
-    B200, fitted to measured per-matrix times of the Llama-3-8B layer shapes
-    (4096 calibration tokens): a fixed 0.08 s, a term in N*C (encode, GPTQ,
-    weight-side Grams) and one in C^2 (Hessians and their factorisations,
-    which run as tensor-core GEMMs).  T_cal scales the Hessian term."""
-    return 0.08 + 5.1e-9 * N * C + 4.1e-9 * C * C * (T_cal / 4096.0) ** 0.5
+    """Seconds to calibrate one N x C matrix (plus one 1024-token dynamic call)
+    on one B200, least-squares fit to measured per-matrix times of the
+    Llama-3-8B layer shapes (4096 calibration tokens; within 0.4 ms of each):
+    a fixed 16 ms, a term in N*C (encode, GPTQ, weight-side Grams) and one
+    in C^2 (Hessians and their factorisations).  T_cal scales the Hessian
+    term."""
+    return 0.0162 + 3.48e-10 * N * C + 6.81e-10 * C * C * (T_cal / 4096.0) ** 0.5
 
 
 def model_jobs(layers: int, shapes: dict = LLAMA3_8B_LAYER) -> list[MatrixJob]:
