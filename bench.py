@@ -123,14 +123,33 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def ncu_traffic():
-    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary."""
+def ncu_summary():
+    """The fused kernel's committed ncu figures (per launch, full size)."""
     try:
         with open(os.path.join(ROOT, "profiles", "convert_c1_16384.json")) as f:
-            d = json.load(f)
-        return d.get("dram_bytes_per_launch_full_size")
+            return json.load(f)
     except (OSError, ValueError):
+        return {}
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary."""
+    return ncu_summary().get("dram_bytes_per_launch_full_size")
+
+
+def issue_roofline(k_ms, sm_mhz, elems):
+    """The fused kernel is bound by instruction issue, not HBM: executed warp
+    instructions per launch (ncu, committed) over the live launch time,
+    against one warp instruction per scheduler per cycle (148 SMs x 4
+    schedulers at the SM clock sampled during the timed region)."""
+    inst = ncu_summary().get("warp_inst_per_launch")
+    if not inst or not sm_mhz:
         return None
+    peak = 148 * 4 * sm_mhz * 1e6
+    achieved = inst / (k_ms * 1e-3)
+    return {"bound": "issue", "achieved": achieved, "peak": peak, "unit": "warp-instructions/s",
+            "frac": achieved / peak, "thread_instr_per_elem": inst * 32 / elems,
+            "source": "smsp__inst_executed.sum per launch from profiles/convert_c1_16384.json"}
 
 
 def cpu_oracle_sample(codes, e4m3, s_dec, rows):
@@ -272,6 +291,7 @@ def run_gpu(args, rank, ws, local_rank):
         "gpu_launches": 2 * K,
         "clocks": clk.summary(w0, w1),
     }
+    line["issue_roofline"] = issue_roofline(k_ms, line["clocks"].get("sm_mhz"), elems)
     if e2e is not None:
         e2e_ms, launches_e2e, h2d, d2h = e2e
         line["e2e"] = {"value": ws * elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": h2d,
