@@ -35,19 +35,27 @@ def load_solution(ref):
     return sol
 
 
-def packed(p: dict):
+def packed(p: dict, rows=None):
     npd = {k: v.float().numpy() for k, v in p.items()}
+    if rows is not None:
+        npd = {k: v[rows] for k, v in npd.items()}
     return oracle.pack_hif4(npd)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", nargs="*", help="regenerate these cases, keep the rest of the file")
     args = ap.parse_args()
     sol = load_solution(args.ref)
     torch.set_num_threads(8)
     out = {}
+    path = os.path.join(HERE, "pipeline_golden.npz")
+    if args.only:
+        out = {k: v for k, v in np.load(path).items() if k.split("/")[0] not in args.only}
     for name in pc.LINEAR_CASES:
+        if args.only and name not in args.only:
+            continue
         wpair, calib, tests, digest = pc.linear_inputs(name)
         t0 = time.time()
         res = sol.hif4_calibration_and_quantize_weight(wpair[0], wpair[1], calib)
@@ -59,7 +67,8 @@ def main():
         out[f"{name}/has_gw"] = np.int64(st["gw"] is not None)
         out[f"{name}/s"] = st["s"].numpy()
         out[f"{name}/order"] = st["order"].numpy() if st["order"] is not None else np.zeros(0, np.int64)
-        meta, codes = packed(res["weight_params"])
+        wrows = pc.code_rows(wpair[0].shape[0])
+        meta, codes = packed(res["weight_params"], wrows)
         out[f"{name}/w_meta"], out[f"{name}/w_codes"] = meta, codes
         W = pc.deq_nvfp4(wpair)
         Wq = pc.deq_dict5(res["weight_params"])
@@ -74,12 +83,14 @@ def main():
             out[f"{name}/t{i}/mse"] = np.float64(((Yq - Y) ** 2).mean())
             out[f"{name}/t{i}/mse_std"] = np.float64(((Ya - Y) ** 2).mean())
             out[f"{name}/t{i}/ref_power"] = np.float64((Y ** 2).mean())
-            m, c = packed(pa)
+            m, c = packed(pa, pc.code_rows(tp[0].shape[0]))
             out[f"{name}/t{i}/meta"], out[f"{name}/t{i}/codes"] = m, c
         print(name, "done in", round(time.time() - t0, 1), "s; mode", st["mode"], "g", st["g"], "tmax", st["tmax"],
               "score", [round(1 - out[f"{name}/t{i}/mse"] / out[f"{name}/t{i}/mse_std"], 4) for i in range(len(tests))])
 
     for name in pc.ATTN_CASES:
+        if args.only and name not in args.only:
+            continue
         (qh, kvh, dh), calib, tests, digest = pc.attn_inputs(name)
         res = sol.hif4_calibration_attention(calib, qh, kvh, dh)
         out[f"{name}/digest"] = np.frombuffer(bytes.fromhex(digest), np.uint8)
@@ -105,7 +116,7 @@ def main():
                 out[f"{name}/t{i}/{role}_meta"], out[f"{name}/t{i}/{role}_codes"] = m, c
         print(name, "rot", qs["rot"], "gq", qs.get("gq", 0),
               "score", [round(1 - out[f"{name}/t{i}/mse"] / out[f"{name}/t{i}/mse_std"], 4) for i in range(len(tests))])
-    np.savez_compressed(os.path.join(HERE, "pipeline_golden.npz"), **out)
+    np.savez_compressed(path, **out)
     print("wrote pipeline_golden.npz")
 
 

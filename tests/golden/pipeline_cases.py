@@ -22,7 +22,18 @@ LINEAR_CASES = {
     "lin_c1024": (256, 1024, (192, 192, 192, 192), (16, 160, 400), 101),
     "lin_c2560": (192, 2560, (160, 160, 160), (48, 520), 202),
     "lin_c4224": (128, 4224, (128, 128, 128), (96,), 303),
+    # the single-linear-layer configuration: W 4096 x 4096, 2048 calibration tokens
+    # (4 samples) with 8 outlier channels x30, test activations T in {10, 128, 512, 1024}
+    "lin_c0": (4096, 4096, (512, 512, 512, 512), (10, 128, 512, 1024), 505),
 }
+
+
+def code_rows(n_rows: int) -> np.ndarray:
+    """Rows whose HiF4 codes the golden file keeps: all of a small output, every
+    32nd row of a large one (the fixture stays small; the mismatch rate is a
+    row sample there)."""
+    step = 1 if n_rows < 1024 else 32
+    return np.arange(0, n_rows, step)
 
 # name: (qh, kvh, dh, calib T list (last = hold-out), test T list, seed)
 ATTN_CASES = {
