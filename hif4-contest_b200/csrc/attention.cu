@@ -9,6 +9,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "tc_gemm.cuh"
 
 namespace hif4x {
 
@@ -119,6 +120,43 @@ __global__ void __launch_bounds__(256) attention_kernel(const float *Q, const fl
   }
 }
 
+// Row softmax of S (qh * T rows of T scores, already scaled) into the TF32
+// hi / lo split of P that the P V product reads: row r of head h goes to
+// P[h][r] (hi) and P[h][T + r] (lo), row pitch kp.  One CTA per row, three
+// passes over the row (max, sum of exponentials, normalise and split).
+__global__ void __launch_bounds__(256) softmax_split_kernel(const float *__restrict__ S, int64_t T, int64_t kp,
+                                                            float *__restrict__ P) {
+  __shared__ float red[8];
+  const int64_t hr = blockIdx.x, h = hr / T, r = hr % T;
+  const float *srow = S + hr * T;
+  float *phi = P + (h * 2 * T + r) * kp, *plo = P + (h * 2 * T + T + r) * kp;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float m = -INFINITY;
+  for (int64_t c = tid; c < T; c += 256) m = fmaxf(m, srow[c]);
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) m = fmaxf(m, red[w]);
+  __syncthreads();
+  float l = 0.0f;
+  for (int64_t c = tid; c < T; c += 256) l += expf(srow[c] - m);
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  l = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; w++) l += red[w];
+  const float inv = 1.0f / l;
+  for (int64_t c = tid; c < T; c += 256) {
+    const float p = expf(srow[c] - m) * inv;
+    const float hi = __uint_as_float(__float_as_uint(p) & 0xffffe000u);
+    phi[c] = hi;
+    plo[c] = __fsub_rn(p, hi);
+  }
+}
+
 // (T, H, D) <-> (H, T, D)
 __global__ void heads_transpose_kernel(const float *in, int64_t T, int64_t H, int64_t D, int inverse, float *out) {
   const int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x;
@@ -137,11 +175,48 @@ __global__ void heads_transpose_kernel(const float *in, int64_t T, int64_t H, in
 
 using namespace hif4x;
 
+// Long sequences on the tensor cores (3xTF32): S_h = scale Q_h K_g^T for all
+// heads in one batched product, the row softmax written as the split P, and
+// O_h = P_h V_g in a second batched product (g = h / (qh / kvh)).
+static int attention_tc(const float *Q, const float *K, const float *V, int64_t T, int qh, int kvh, int dh,
+                        float *O, cudaStream_t s) {
+  const int64_t kpd = (dh + 3) / 4 * 4, kpt = (T + 3) / 4 * 4;
+  // every sub-buffer a multiple of 4 floats: the tensor maps need 16-byte-aligned bases
+  const int64_t nq = (int64_t)qh * 2 * T * kpd, nk = (int64_t)kvh * 2 * T * kpd, ns = ((int64_t)qh * T * T + 3) / 4 * 4;
+  const int64_t np = (int64_t)qh * 2 * T * kpt, nv = (int64_t)kvh * 2 * dh * kpt;
+  float *ws = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void **>(&ws), (size_t)(nq + nk + ns + np + nv) * sizeof(float), s) !=
+      cudaSuccess)
+    return HIF4X_ERR_LAUNCH;
+  float *Qs = ws, *Ks = Qs + nq, *Sm = Ks + nk, *Ps = Sm + ns, *Vs = Ps + np;
+  const int rep = qh / kvh;
+  const float scale = 1.0f / sqrtf((float)dh);
+  int st = tc::split_operand(Q, (int64_t)qh * dh, 1, T, dh, dh, qh, Qs, kpd, s);
+  if (st == HIF4X_OK) st = tc::split_operand(K, (int64_t)kvh * dh, 1, T, dh, dh, kvh, Ks, kpd, s);
+  if (st == HIF4X_OK) st = tc::gemm_split(Qs, qh, Ks, kvh, T, T, dh, kpd, scale, 0.0f, Sm, T, T * T, qh, rep, 0, s);
+  if (st == HIF4X_OK) {
+    softmax_split_kernel<<<(unsigned)(qh * T), 256, 0, s>>>(Sm, T, kpt, Ps);
+    if (cudaGetLastError() != cudaSuccess) st = HIF4X_ERR_LAUNCH;
+  }
+  if (st == HIF4X_OK) st = tc::split_operand(V, (int64_t)kvh * dh, 0, dh, T, dh, kvh, Vs, kpt, s);
+  if (st == HIF4X_OK)
+    st = tc::gemm_split(Ps, qh, Vs, kvh, T, dh, T, kpt, 1.0f, 0.0f, O, (int64_t)qh * dh, dh, qh, rep, 0, s);
+  cudaFreeAsync(ws, s);
+  return st;
+}
+
+// Sequences from this length on take the tensor-core form.
+static const int64_t kAttnTcMinT = 1024;
+
 extern "C" int hif4x_attention(const float *Q, const float *K, const float *V, int64_t T, int qh, int kvh, int dh,
                                float *O, void *stream) {
   if (T < 0 || qh <= 0 || kvh <= 0 || qh % kvh != 0 || dh <= 0 || dh > ADH) return HIF4X_ERR_ARG;
   if (T == 0) return HIF4X_OK;
   if (!Q || !K || !V || !O) return HIF4X_ERR_ARG;
+  if (T >= kAttnTcMinT && qh * T <= INT32_MAX) {
+    const int st = attention_tc(Q, K, V, T, qh, kvh, dh, O, (cudaStream_t)stream);
+    if (st != HIF4X_ERR_UNSUPPORTED) return st;
+  }
   const size_t smem = sizeof(float) * (2 * AT * (ADH + 1) + AT * ADH + AT * (AT + 1));
   if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return HIF4X_ERR_LAUNCH;

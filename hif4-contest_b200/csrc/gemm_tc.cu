@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tc_gemm.cuh"
 
 namespace hif4x {
 namespace tc {
@@ -132,10 +133,14 @@ struct TcArgs {
   float *C;
   int64_t ldc;
   int a_lo, b_lo;   // row of the lo half in each split operand (hi rows come first)
-  int tm, tn;       // tile rows / columns
+  int tm, tn;       // tile rows / columns of one product
   int lower;        // 1: only tiles on or below the diagonal (square C)
   int vec;          // 1: C rows take 16-byte stores
-  int64_t ntiles;
+  int64_t ntiles;   // batch * tiles_per
+  int64_t tiles_per;
+  int a_bstride, b_bstride;   // split-operand rows between products (2M, 2N)
+  int b_div;                  // product b reads B's product b / b_div
+  int64_t c_bstride;          // C elements between products
 };
 
 // Tile t of the visiting order -> (tile row, tile column).  Bands of GROUP
@@ -223,9 +228,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     if (lane == 0) {
       int64_t g = 0;   // stage fills issued so far (a failed wait leaves g unissued)
       for (int64_t t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
+        const int64_t b = t / args.tiles_per;
         int ti, tj;
-        tile_coords(args, t, ti, tj);
-        const int m0 = ti * BM, n0 = tj * BN;
+        tile_coords(args, t - b * args.tiles_per, ti, tj);
+        const int m0 = (int)b * args.a_bstride + ti * BM, n0 = (int)(b / args.b_div) * args.b_bstride + tj * BN;
         for (int kt = 0; kt < nk; kt++, g++) {
           const int s = (int)(g % STAGES);
           if (g >= STAGES) ok = mbar_wait(&empty[s], (uint32_t)(((g / STAGES) - 1) & 1));
@@ -291,8 +297,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld below is warp-collective
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;");
+      const int64_t b = t / args.tiles_per;
       int ti, tj;
-      tile_coords(args, t, ti, tj);
+      tile_coords(args, t - b * args.tiles_per, ti, tj);
       const int64_t row = (int64_t)ti * BM + quarter * 32 + lane;
       const int64_t n0 = (int64_t)tj * BN;
       uint32_t r[BN];
@@ -317,7 +324,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       asm volatile("tcgen05.fence::before_thread_sync;");
       mbar_arrive(&tempty[buf]);
       if (row < args.M) {
-        float *crow = args.C + row * args.ldc;
+        float *crow = args.C + b * args.c_bstride + row * args.ldc;
         const float alpha = args.alpha, beta = args.beta;
 #pragma unroll
         for (int c = 0; c < BN / 32; c++) {
@@ -366,10 +373,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 //   dst[r * kp + k] = hi(x(r, k)),  dst[(R + r) * kp + k] = lo(x(r, k))
 // where x(r, k) = src[r * ld + k] (k_contig) or src[k * ld + r].  32 x 32
 // tiles; the transposing form goes through shared memory so that both the
-// loads and the stores are coalesced.
+// loads and the stores are coalesced.  blockIdx.z indexes a batch of
+// operands src_bstride apart, written 2 R kp apart.
 __global__ void split_tf32_kernel(const float *__restrict__ src, int64_t ld, int k_contig, int64_t R, int64_t K,
-                                  float *__restrict__ dst, int64_t kp) {
+                                  int64_t src_bstride, float *__restrict__ dst, int64_t kp) {
   __shared__ float tile[32][33];
+  src += (int64_t)blockIdx.z * src_bstride;
+  dst += (int64_t)blockIdx.z * 2 * R * kp;
   const int64_t k0 = (int64_t)blockIdx.x * 32, r0 = (int64_t)blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
   if (!k_contig) {
@@ -447,13 +457,56 @@ static int device_sms(int dev) {
   return sms[dev];
 }
 
-static int split_operand(const float *src, int64_t ld, int k_contig, int64_t R, int64_t K, float *dst, int64_t kp,
-                         cudaStream_t s) {
+int split_operand(const float *src, int64_t ld, int k_contig, int64_t R, int64_t K, int64_t src_bstride,
+                  int batch, float *dst, int64_t kp, cudaStream_t s) {
   const int64_t gy = (R + 31) / 32;
-  if (gy > 65535) return HIF4X_ERR_UNSUPPORTED;
-  dim3 grid((unsigned)((K + 31) / 32), (unsigned)gy);
-  split_tf32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, k_contig, R, K, dst, kp);
+  if (gy > 65535 || batch < 1 || batch > 65535) return HIF4X_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)((K + 31) / 32), (unsigned)gy, (unsigned)batch);
+  split_tf32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, k_contig, R, K, src_bstride, dst, kp);
   return HIF4X_OK;
+}
+
+int gemm_split(const float *As, int a_products, const float *Bs, int b_products, int64_t M, int64_t N, int64_t K,
+               int64_t kp, float alpha, float beta, float *C, int64_t ldc, int64_t c_bstride, int batch, int b_div,
+               int lower, cudaStream_t s) {
+  if (M <= 0 || N <= 0 || K <= 0 || batch < 1 || b_div < 1 || (batch - 1) / b_div >= b_products ||
+      batch > a_products)
+    return HIF4X_ERR_ARG;
+  if (2 * M * a_products > INT32_MAX || 2 * N * b_products > INT32_MAX) return HIF4X_ERR_UNSUPPORTED;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return HIF4X_ERR_LAUNCH;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, As, K, 2 * M * a_products, kp) || !make_map(&mb, Bs, K, 2 * N * b_products, kp))
+    return HIF4X_ERR_UNSUPPORTED;
+  TcArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.alpha = alpha;
+  args.beta = beta;
+  args.C = C;
+  args.ldc = ldc;
+  args.a_lo = (int)M;
+  args.b_lo = (int)N;
+  args.tm = (int)((M + BM - 1) / BM);
+  args.tn = (int)((N + BN - 1) / BN);
+  args.lower = (lower && M == N) ? 1 : 0;
+  args.vec = ((ldc & 3) == 0 && (c_bstride & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0) ? 1 : 0;
+  args.tiles_per = args.lower ? (int64_t)args.tm * (args.tm + 1) / 2 : (int64_t)args.tm * args.tn;
+  args.ntiles = args.tiles_per * batch;
+  args.a_bstride = (int)(2 * M);
+  args.b_bstride = (int)(2 * N);
+  args.b_div = b_div;
+  args.c_bstride = c_bstride;
+  static std::once_flag attr_once;
+  std::call_once(attr_once, [] {
+    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  const int64_t grid = std::min<int64_t>(args.ntiles, sms);
+  gemm_tc_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, s>>>(ma, mb, args);
+  return cudaGetLastError() == cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
 }
 
 }  // namespace tc
@@ -480,53 +533,21 @@ int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alph
                      const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return HIF4X_ERR_ARG;
   cudaStream_t s = (cudaStream_t)stream;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return HIF4X_ERR_LAUNCH;
-  const int sms = tc::device_sms(dev);
-  if (sms <= 0) return HIF4X_ERR_LAUNCH;
   const int64_t kp = (K + 3) / 4 * 4;   // 16-byte row pitch for the tensor maps
   // operand (r, k) is K-contiguous in memory for A when ta == 0 and for B when tb == 1
   const int a_kc = ta ? 0 : 1, b_kc = tb ? 1 : 0;
   const bool same = A == B && lda == ldb && a_kc == b_kc && M == N;
-  if (2 * (M + N) > INT32_MAX) return HIF4X_ERR_UNSUPPORTED;   // TMA row coordinates are 32-bit
   const int64_t a_floats = 2 * kp * M, b_floats = same ? 0 : 2 * kp * N;
   float *ws = nullptr;
   if (cudaMallocAsync(reinterpret_cast<void **>(&ws), (size_t)(a_floats + b_floats) * sizeof(float), s) !=
       cudaSuccess)
     return HIF4X_ERR_LAUNCH;
   float *As = ws, *Bs = same ? ws : ws + a_floats;
-  int st = tc::split_operand(A, lda, a_kc, M, K, As, kp, s);
-  if (st == HIF4X_OK && !same) st = tc::split_operand(B, ldb, b_kc, N, K, Bs, kp, s);
-  CUtensorMap ma, mb;
-  if (st == HIF4X_OK && (!tc::make_map(&ma, As, K, 2 * M, kp) || !tc::make_map(&mb, Bs, K, 2 * N, kp)))
-    st = HIF4X_ERR_UNSUPPORTED;
-  if (st == HIF4X_OK) {
-    tc::TcArgs args{};
-    args.M = M;
-    args.N = N;
-    args.K = K;
-    args.alpha = alpha;
-    args.beta = beta;
-    args.C = C;
-    args.ldc = ldc;
-    args.a_lo = (int)M;
-    args.b_lo = (int)N;
-    args.tm = (int)((M + tc::BM - 1) / tc::BM);
-    args.tn = (int)((N + tc::BN - 1) / tc::BN);
-    args.lower = (lower && M == N) ? 1 : 0;
-    args.vec = ((ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0) ? 1 : 0;
-    args.ntiles = args.lower ? (int64_t)args.tm * (args.tm + 1) / 2 : (int64_t)args.tm * args.tn;
-    static std::once_flag attr_once;
-    std::call_once(attr_once, [] {
-      cudaFuncSetAttribute(tc::gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
-    });
-    const int64_t grid = std::min<int64_t>(args.ntiles, sms);
-    tc::gemm_tc_kernel<<<(unsigned)grid, tc::THREADS, tc::SMEM_BYTES, s>>>(ma, mb, args);
-  }
-  const cudaError_t launch = cudaGetLastError();
+  int st = tc::split_operand(A, lda, a_kc, M, K, 0, 1, As, kp, s);
+  if (st == HIF4X_OK && !same) st = tc::split_operand(B, ldb, b_kc, N, K, 0, 1, Bs, kp, s);
+  if (st == HIF4X_OK) st = tc::gemm_split(As, 1, Bs, 1, M, N, K, kp, alpha, beta, C, ldc, 0, 1, 1, lower, s);
   cudaFreeAsync(ws, s);
-  if (st != HIF4X_OK) return st;
-  return launch == cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
+  return st;
 }
 
 // Synchronises the stream and reports (then clears) the sticky device status

@@ -125,15 +125,19 @@ def test_refine_rows_vs_oracle(T, C):
     assert float(e1) <= float(e0)
 
 
-def test_attention_vs_torch():
-    T, qh, kvh, dh = 200, 8, 2, 128
+@pytest.mark.parametrize("T,qh,kvh", [(200, 8, 2), (1030, 8, 2), (2048, 16, 4)])
+def test_attention_vs_torch(T, qh, kvh):
+    """SIMT form below 1024 tokens, tensor-core form (batched 3xTF32 products
+    around a row softmax) from 1024 on, including a ragged length."""
+    dh = 128
     q, k, v = rnd(T, qh * dh, seed=1), rnd(T, kvh * dh, seed=2), rnd(T, kvh * dh, seed=3)
     got = att.attention_out(q, k, v, qh, kvh, dh)
     qf = q.double().view(T, qh, dh).transpose(0, 1)
-    kf = k.double().view(T, kvh, dh).transpose(0, 1).repeat_interleave(4, 0)
-    vf = v.double().view(T, kvh, dh).transpose(0, 1).repeat_interleave(4, 0)
+    kf = k.double().view(T, kvh, dh).transpose(0, 1).repeat_interleave(qh // kvh, 0)
+    vf = v.double().view(T, kvh, dh).transpose(0, 1).repeat_interleave(qh // kvh, 0)
     ref = (torch.softmax(qf @ kf.transpose(1, 2) / dh ** 0.5, -1) @ vf).transpose(0, 1).reshape(T, -1)
     assert float((got.double() - ref).abs().max()) < 1e-4
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
 
 
 def test_helpers_vs_torch():
