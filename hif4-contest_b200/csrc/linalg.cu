@@ -1014,8 +1014,8 @@ static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_
   return hif4x_gemm(0, 0, n2, n1, n2, -1.0f, A22, ld, 0, work, n1, 0, 0.0f, A21, ld, 0, 1, s);
 }
 
-extern "C" int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
-                                    int *info_dev, void *stream) {
+extern "C" int hif4x_chol_upper_inv_async(const float *H, int64_t n, int64_t batch, float damp, float *U,
+                                          float *work, int *info_dev, void *stream) {
   if (n <= 0 || batch <= 0 || !H || !U || !work || !info_dev) return HIF4X_ERR_ARG;
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t nn = n * n;
@@ -1033,6 +1033,14 @@ extern "C" int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, fl
     reverse_flat_kernel<<<nblk((nn + 1) / 2, 256), 256, 0, s>>>(Inv, nn);
   }
   HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
+                                    int *info_dev, void *stream) {
+  const int st = hif4x_chol_upper_inv_async(H, n, batch, damp, U, work, info_dev, stream);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
   int info = 0;
   if (cudaMemcpyAsync(&info, info_dev, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
       cudaStreamSynchronize(s) != cudaSuccess)

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, list] = {
     "hif4x_unpack_dict5": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp],
     "hif4x_gemm": [i32, i32, i64, i64, i64, f32, vp, i64, i64, vp, i64, i64, f32, vp, i64, i64, i64, vp],
     "hif4x_chol_upper_inv": [vp, i64, i64, f32, vp, vp, vp, vp],
+    "hif4x_chol_upper_inv_async": [vp, i64, i64, f32, vp, vp, vp, vp],
     "hif4x_gptq": [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp],
     "hif4x_refine_rows": [vp, vp, vp, vp, i64, i64, i32, vp, vp],
     "hif4x_col_abs_sum": [vp, i64, i64, vp, i32, vp, vp],

@@ -86,6 +86,32 @@ def chol_upper_inv(H: torch.Tensor, damp: float = GPTQ_DAMP) -> torch.Tensor | N
     return U if batched else U[0]
 
 
+class CholLaunch:
+    """A damped Cholesky-inverse launched on a stream (chol_upper_inv_launch);
+    finish() reads its status on the current stream, which must have waited
+    for the launching one."""
+
+    def __init__(self, U, info, keep):
+        self.U, self.info, self._keep = U, info, keep
+
+    def finish(self) -> torch.Tensor | None:
+        ok = int(self.info.item()) == 0
+        self._keep = None
+        return self.U if ok else None
+
+
+def chol_upper_inv_launch(H: torch.Tensor, damp: float = GPTQ_DAMP) -> CholLaunch:
+    """chol_upper_inv on the current stream without synchronising it."""
+    batched = H.dim() == 3
+    Hb = (H if batched else H.unsqueeze(0)).contiguous()
+    nb, n = Hb.shape[0], Hb.shape[1]
+    U = torch.empty_like(Hb)
+    work = torch.empty(2 * n * n, dtype=torch.float32, device=H.device)
+    info = torch.zeros(1, dtype=torch.int32, device=H.device)
+    L.call("hif4x_chol_upper_inv_async", L.ptr(Hb), n, nb, L.f32(damp), L.ptr(U), L.ptr(work), L.ptr(info), _s(H))
+    return CholLaunch(U if batched else U[0], info, (Hb, work))
+
+
 def gptq(X: torch.Tensor, unit: torch.Tensor, U: torch.Tensor) -> torch.Tensor:
     """_gptq_quantize_values (R, C) or _gptq_quantize_batched (B, R, n) with
     U (n, n) shared or (B, n, n) per batch element."""
@@ -171,6 +197,14 @@ def mse(A: torch.Tensor, B: torch.Tensor | None = None) -> float:
     """mean((A - B)^2) accumulated in double."""
     n = A.numel()
     return _reduce(A, B, 0) / max(n, 1)
+
+
+def sq_sum_async(A: torch.Tensor) -> torch.Tensor:
+    """sum(A^2) in double as a one-element device tensor (no synchronisation)."""
+    out = torch.empty(1, dtype=torch.float64, device=A.device)
+    work = torch.empty(1024, dtype=torch.float64, device=A.device)
+    L.call("hif4x_reduce", L.ptr(A), None, A.numel(), 0, L.ptr(out), L.ptr(work), _s(A))
+    return out
 
 
 def abs_sum_f64(A: torch.Tensor) -> float:

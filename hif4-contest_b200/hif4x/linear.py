@@ -87,6 +87,17 @@ class _Phases:
                 for i in range(len(self.marks) - 1)}
 
 
+_SIDE: dict = {}
+
+
+def _side_stream(dev) -> torch.cuda.Stream:
+    """A second stream per device for independent calibration branches."""
+    key = str(dev)
+    if key not in _SIDE:
+        _SIDE[key] = torch.cuda.Stream(device=dev)
+    return _SIDE[key]
+
+
 def _randperm(n: int, k: int, dev) -> torch.Tensor:
     """torch.randperm(n)[:k] on the host generator (the reference's RNG call)."""
     return torch.randperm(n)[:min(n, k)].to(dev)
@@ -184,24 +195,34 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         rsub = _randperm(R, 256, dev)
         xh_last = acts_s[-1]
         sub = _randperm(xh_last.shape[0], 128, dev)
-        spaces = []
-        for md in (0, 1):
-            Hs = torch.zeros(C, C, dtype=torch.float32, device=dev)
-            for a in acts_s[:-1]:
-                la.gram(tf(a, md), out=Hs, accumulate=True)
-            spaces.append(la.chol_upper_inv(Hs))
-            del Hs
         xh_sub = la.gather_rows(xh_last, sub)
-        cand = []
-        for md, U in enumerate(spaces):
-            if U is None:
-                cand.append(float("inf"))
-                continue
-            w_rsub = tf(la.gather_rows(w_s, rsub), md)
-            pp = _encode_fast(w_rsub)
-            qq = la.gptq(w_rsub, pp["unit"], U)
-            xt = tf(xh_sub, md)
-            cand.append(_resid_mse(xt, qq, w_rsub))
+        w_sub = la.gather_rows(w_s, rsub)
+        # the two spaces are independent: each runs its Hessian, Cholesky-inverse
+        # and GPTQ proxy on its own stream (the factorisations are latency-bound
+        # for much of their run and overlap well); results are read after both
+        main = torch.cuda.current_stream(dev)
+        side = _side_stream(dev)
+        side.wait_stream(main)
+        runs = []
+        for md, stream in ((0, main), (1, side)):
+            with torch.cuda.stream(stream):
+                Hs = torch.zeros(C, C, dtype=torch.float32, device=dev)
+                for a in acts_s[:-1]:
+                    la.gram(tf(a, md), out=Hs, accumulate=True)
+                chol = la.chol_upper_inv_launch(Hs)
+                del Hs
+                w_rsub = tf(w_sub, md)
+                qq = la.gptq(w_rsub, _encode_fast(w_rsub)["unit"], chol.U)
+                xt = tf(xh_sub, md)
+                runs.append((chol, la.sq_sum_async(_resid(xt, qq, w_rsub)), xt.shape[0] * w_rsub.shape[0]))
+        main.wait_stream(side)
+        spaces, cand = [], []
+        for chol, sq, n in runs:
+            U = chol.finish()
+            if U is not None:
+                U.record_stream(main)
+            spaces.append(U)
+            cand.append(float("inf") if U is None else float(sq.item()) / max(n, 1))
         mode = min(range(2), key=lambda i: (cand[i], i)) if not all(math.isnan(c) for c in cand) else 0
         if mode == 1 and spaces[1] is None:
             mode = 0

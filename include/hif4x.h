@@ -198,6 +198,13 @@ int hif4x_device_status(void *stream);
 int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
                          int *info_dev, void *stream);
 
+/* hif4x_chol_upper_inv without the synchronisation: launches the work on
+ * `stream` and returns; *info_dev becomes nonzero (once the stream reaches
+ * it) where hif4x_chol_upper_inv would return HIF4X_NOT_PD.  Lets a caller
+ * run independent factorisations on several streams. */
+int hif4x_chol_upper_inv_async(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
+                               int *info_dev, void *stream);
+
 /* Allocation-free twin of hif4x_chol_upper_inv (no counterpart in the
  * reference).  For callers that cannot allocate device memory at the call --
  * a host whose device memory another runtime plans up front, or a
