@@ -98,6 +98,27 @@ def _side_stream(dev) -> torch.cuda.Stream:
     return _SIDE[key]
 
 
+def _act_factor_launch(q: torch.Tensor):
+    """Ha = q^T q, act order = argsort(diag Ha) descending, and the damped
+    Cholesky-inverse of the permuted Ha launched on the current stream
+    (solution.py:941-951)."""
+    Ha = la.gram(q)
+    order = la.argsort_desc(la.diag(Ha))
+    return Ha, order, la.chol_upper_inv_launch(la.permute_sym(Ha, order))
+
+
+def _act_factor_finish(spec, stream):
+    """(Ua, order) from _act_factor_launch; the unpermuted factorisation when
+    the permuted one is not positive definite, as the reference falls back."""
+    Ha, order, chol = spec
+    Ua = chol.finish()
+    if Ua is None:
+        return la.chol_upper_inv(Ha), None
+    Ua.record_stream(stream)
+    order.record_stream(stream)
+    return Ua, order
+
+
 def _randperm(n: int, k: int, dev) -> torch.Tensor:
     """torch.randperm(n)[:k] on the host generator (the reference's RNG call)."""
     return torch.randperm(n)[:min(n, k)].to(dev)
@@ -235,6 +256,16 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     res_q = None   # xh_pick @ (q_used - w_final)^T, the hold-out residual of the weight choice
     # ---- searched encode + hold-out-guarded GPTQ (solution.py:921-934)
     weight_params, q_used, unit = _search(w_final)
+    # the activation-side factorisation depends on the guard's outcome only
+    # through q_used: start it for the searched encode on the side stream while
+    # the weight GPTQ runs, and redo it below only if GPTQ wins
+    spec = None
+    if xh_pick is not None:
+        main = torch.cuda.current_stream(dev)
+        side = _side_stream(dev)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            spec = _act_factor_launch(q_used)
     gptq_w = False
     if xh_pick is not None and Uw is not None:
         q_g = la.gptq(w_final, unit, Uw)
@@ -254,13 +285,12 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     # ---- activation-side GPTQ with act-order (solution.py:936-976)
     u_act, gptq_act, order = None, 0, None
     if xh_pick is not None:
-        Ha = la.gram(q_used)
-        order = la.argsort_desc(la.diag(Ha))
-        Ua = la.chol_upper_inv(la.permute_sym(Ha, order))
-        if Ua is None:
-            order = None
-            Ua = la.chol_upper_inv(Ha)
-        del Ha
+        main = torch.cuda.current_stream(dev)
+        main.wait_stream(_side_stream(dev))
+        if spec is None or gptq_w:
+            spec = _act_factor_launch(q_used)
+        Ua, order = _act_factor_finish(spec, main)
+        spec = None
         if Ua is not None:
             p_r, xr, unit_x = _search(xh_pick)
             if order is not None:
