@@ -193,14 +193,14 @@ static int attention_tc(const float *Q, const float *K, const float *V, int64_t 
   const float scale = 1.0f / sqrtf((float)dh);
   int st = tc::split_operand(Q, (int64_t)qh * dh, 1, T, dh, dh, qh, Qs, kpd, s);
   if (st == HIF4X_OK) st = tc::split_operand(K, (int64_t)kvh * dh, 1, T, dh, dh, kvh, Ks, kpd, s);
-  if (st == HIF4X_OK) st = tc::gemm_split(Qs, qh, Ks, kvh, T, T, dh, kpd, scale, 0.0f, Sm, T, T * T, qh, rep, 0, s);
+  if (st == HIF4X_OK) st = tc::gemm_split(Qs, qh, Ks, kvh, T, T, dh, kpd, scale, 0.0f, Sm, T, T * T, qh, rep, 0, 0, s);
   if (st == HIF4X_OK) {
     softmax_split_kernel<<<(unsigned)(qh * T), 256, 0, s>>>(Sm, T, kpt, Ps);
     if (cudaGetLastError() != cudaSuccess) st = HIF4X_ERR_LAUNCH;
   }
   if (st == HIF4X_OK) st = tc::split_operand(V, (int64_t)kvh * dh, 0, dh, T, dh, kvh, Vs, kpt, s);
   if (st == HIF4X_OK)
-    st = tc::gemm_split(Ps, qh, Vs, kvh, T, dh, T, kpt, 1.0f, 0.0f, O, (int64_t)qh * dh, dh, qh, rep, 0, s);
+    st = tc::gemm_split(Ps, qh, Vs, kvh, T, dh, T, kpt, 1.0f, 0.0f, O, (int64_t)qh * dh, dh, qh, rep, 0, 0, s);
   cudaFreeAsync(ws, s);
   return st;
 }

@@ -141,7 +141,23 @@ struct TcArgs {
   int a_bstride, b_bstride;   // split-operand rows between products (2M, 2N)
   int b_div;                  // product b reads B's product b / b_div
   int64_t c_bstride;          // C elements between products
+  int kmode;                  // triangular operand: K-steps a tile may skip (tile_krange)
 };
+
+// K-steps [kb, ke) that can be nonzero for output tile (ti, tj) when one
+// operand is triangular (its other entries are zeros in memory, so skipping
+// them only saves work):
+//   kmode 1: B(n, k) = 0 for k > n  ->  k < (tj + 1) * BN
+//   kmode 2: B(n, k) = 0 for k < n  ->  k >= tj * BN
+//   kmode 3: A(m, k) = 0 for k > m  ->  k < (ti + 1) * BM
+// At least one step is always kept, so every accumulator is written.
+__device__ __forceinline__ void tile_krange(const TcArgs &a, int ti, int tj, int nk, int &kb, int &ke) {
+  kb = 0;
+  ke = nk;
+  if (a.kmode == 1) ke = min(nk, (tj + 1) * (BN / BK));
+  else if (a.kmode == 2) kb = min(nk - 1, tj * (BN / BK));
+  else if (a.kmode == 3) ke = min(nk, (ti + 1) * (BM / BK));
+}
 
 // Tile t of the visiting order -> (tile row, tile column).  Bands of GROUP
 // tile-rows; inside a band, column by column.  With `lower` (tm == tn) only
@@ -232,7 +248,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         int ti, tj;
         tile_coords(args, t - b * args.tiles_per, ti, tj);
         const int m0 = (int)b * args.a_bstride + ti * BM, n0 = (int)(b / args.b_div) * args.b_bstride + tj * BN;
-        for (int kt = 0; kt < nk; kt++, g++) {
+        int kb, ke;
+        tile_krange(args, ti, tj, nk, kb, ke);
+        for (int kt = kb; kt < ke; kt++, g++) {
           const int s = (int)(g % STAGES);
           if (g >= STAGES) ok = mbar_wait(&empty[s], (uint32_t)(((g / STAGES) - 1) & 1));
           if (!ok) break;
@@ -262,7 +280,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;");
         const uint32_t d = tmem + (uint32_t)(buf * BN);
-        for (int kt = 0; kt < nk; kt++, g++) {
+        int kb = 0, ke = nk;
+        if (args.kmode != 0) {
+          const int64_t b = t / args.tiles_per;
+          int ti, tj;
+          tile_coords(args, t - b * args.tiles_per, ti, tj);
+          tile_krange(args, ti, tj, nk, kb, ke);
+        }
+        for (int kt = kb; kt < ke; kt++, g++) {
           const int s = (int)(g % STAGES);
           ok = mbar_wait(&full[s], (uint32_t)((g / STAGES) & 1));
           if (!ok) break;
@@ -274,7 +299,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           for (int j = 0; j < BK / 8; j++) {
             const uint64_t dah = kmajor_desc(a_hi, j), dal = kmajor_desc(a_lo, j);
             const uint64_t dbh = kmajor_desc(b_hi, j), dbl = kmajor_desc(b_lo, j);
-            mma_tf32(d, dah, dbh, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+            mma_tf32(d, dah, dbh, idesc, (kt > kb || j > 0) ? 1u : 0u);
             mma_tf32(d, dah, dbl, idesc, 1u);
             mma_tf32(d, dal, dbh, idesc, 1u);
           }
@@ -468,7 +493,7 @@ int split_operand(const float *src, int64_t ld, int k_contig, int64_t R, int64_t
 
 int gemm_split(const float *As, int a_products, const float *Bs, int b_products, int64_t M, int64_t N, int64_t K,
                int64_t kp, float alpha, float beta, float *C, int64_t ldc, int64_t c_bstride, int batch, int b_div,
-               int lower, cudaStream_t s) {
+               int lower, int kmode, cudaStream_t s) {
   if (M <= 0 || N <= 0 || K <= 0 || batch < 1 || b_div < 1 || (batch - 1) / b_div >= b_products ||
       batch > a_products)
     return HIF4X_ERR_ARG;
@@ -500,6 +525,7 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
   args.b_bstride = (int)(2 * N);
   args.b_div = b_div;
   args.c_bstride = c_bstride;
+  args.kmode = (kmode >= 0 && kmode <= 3) ? kmode : 0;
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
@@ -515,22 +541,25 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
 using namespace hif4x;
 
 int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
-                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream);
+                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, int kmode,
+                     void *stream);
 
 extern "C" int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
                              int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
                              void *stream) {
-  return hif4x_gemm_tc_ex(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, 0, stream);
+  return hif4x_gemm_tc_ex(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, 0, 0, stream);
 }
 
 // Same, optionally restricted to output tiles on or below the diagonal
-// (lower != 0 and M == N; a diagonal tile is written whole).  The split
+// (lower != 0 and M == N; a diagonal tile is written whole) and to the
+// K-steps a triangular operand leaves nonzero (kmode, see tile_krange).  The split
 // operands live in a stream-ordered allocation of 2 * kp * (M + N) floats
 // (2 * kp * M when A and B are the same operand, as in X^T X or L L^T).
 // Returns HIF4X_ERR_UNSUPPORTED when a tensor map cannot be built, so the
 // caller can take the SIMT kernel instead.
 int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
-                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream) {
+                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, int kmode,
+                     void *stream) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return HIF4X_ERR_ARG;
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t kp = (K + 3) / 4 * 4;   // 16-byte row pitch for the tensor maps
@@ -545,7 +574,7 @@ int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alph
   float *As = ws, *Bs = same ? ws : ws + a_floats;
   int st = tc::split_operand(A, lda, a_kc, M, K, 0, 1, As, kp, s);
   if (st == HIF4X_OK && !same) st = tc::split_operand(B, ldb, b_kc, N, K, 0, 1, Bs, kp, s);
-  if (st == HIF4X_OK) st = tc::gemm_split(As, 1, Bs, 1, M, N, K, kp, alpha, beta, C, ldc, 0, 1, 1, lower, s);
+  if (st == HIF4X_OK) st = tc::gemm_split(As, 1, Bs, 1, M, N, K, kp, alpha, beta, C, ldc, 0, 1, 1, lower, kmode, s);
   cudaFreeAsync(ws, s);
   return st;
 }

@@ -869,7 +869,8 @@ extern "C" int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, 
                                int64_t lda, int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta,
                                float *C, int64_t ldc, int64_t strideC, int64_t batch, void *stream);
 int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
-                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, void *stream);
+                     const float *B, int64_t ldb, float beta, float *C, int64_t ldc, int lower, int kmode,
+                     void *stream);
 static int gemm_simt_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
                         int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream);
@@ -881,7 +882,7 @@ static const int64_t kSmallMaxMacs = int64_t(1) << 27;
 
 static int gemm_dispatch(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
                          int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
-                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream);
+                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream, int kmode = 0);
 
 static bool tc_disabled() {
   static const bool off = [] {
@@ -903,9 +904,9 @@ extern "C" int hif4x_gemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float
 
 static int gemm_dispatch(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,
                          int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
-                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream) {
+                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream, int kmode) {
   if (batch == 1 && K >= 64 && M * N * K >= kTcMinMacs && !tc_disabled()) {
-    const int st = hif4x_gemm_tc_ex(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, lower, stream);
+    const int st = hif4x_gemm_tc_ex(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, lower, kmode, stream);
     if (st != HIF4X_ERR_UNSUPPORTED) return st;
   }
   return gemm_simt_ex(ta, tb, M, N, K, alpha, A, lda, strideA, B, ldb, strideB, beta, C, ldc, strideC, batch, lower,
@@ -986,15 +987,17 @@ static int potrf_inv_rec(float *A, int64_t n, int64_t ld, float *Inv, int64_t ld
   float *I11 = Inv, *I21 = Inv + n1 * ldi, *I22 = Inv + n1 * ldi + n1;
   int st = potrf_inv_rec(A, n1, ld, I11, ldi, info_dev, work, s);
   if (st) return st;
-  st = gemm_dispatch(0, 1, n2, n1, n1, 1.0f, A21, ld, 0, I11, ldi, 0, 0.0f, I21, ldi, 0, 1, 0, s);
+  // L11^-1 and L22^-1 are lower triangular (zeros above the diagonal in
+  // memory): kmode lets the tensor-core products skip their zero K-steps
+  st = gemm_dispatch(0, 1, n2, n1, n1, 1.0f, A21, ld, 0, I11, ldi, 0, 0.0f, I21, ldi, 0, 1, 0, s, 1);
   if (st) return st;
   st = gemm_dispatch(0, 1, n2, n2, n1, -1.0f, I21, ldi, 0, I21, ldi, 0, 1.0f, A22, ld, 0, 1, 1, s);
   if (st) return st;
   st = potrf_inv_rec(A22, n2, ld, I22, ldi, info_dev, work, s);
   if (st) return st;
-  st = gemm_dispatch(0, 0, n2, n1, n1, 1.0f, I21, ldi, 0, I11, ldi, 0, 0.0f, work, n1, 0, 1, 0, s);
+  st = gemm_dispatch(0, 0, n2, n1, n1, 1.0f, I21, ldi, 0, I11, ldi, 0, 0.0f, work, n1, 0, 1, 0, s, 2);
   if (st) return st;
-  return gemm_dispatch(0, 0, n2, n1, n2, -1.0f, I22, ldi, 0, work, n1, 0, 0.0f, I21, ldi, 0, 1, 0, s);
+  return gemm_dispatch(0, 0, n2, n1, n2, -1.0f, I22, ldi, 0, work, n1, 0, 0.0f, I21, ldi, 0, 1, 0, s, 3);
 }
 
 // In-place inverse of a lower-triangular n x n block at A (leading dim ld):

@@ -16,9 +16,12 @@ int split_operand(const float *src, int64_t ld, int k_contig, int64_t R, int64_t
 // C_b = alpha * A_b B_{b / b_div}^T + beta * C_b for b < batch, with A_b the
 // split operand b of As (M rows, a_products of them) and B_g the split
 // operand g of Bs (N rows); C_b at C + b * c_bstride, leading dimension ldc.
+// lower: only output tiles on or below the diagonal; kmode: skip the K-steps
+// a triangular operand leaves zero (1: B(n,k)=0 for k>n, 2: B(n,k)=0 for
+// k<n, 3: A(m,k)=0 for k>m; 0: none).
 int gemm_split(const float *As, int a_products, const float *Bs, int b_products, int64_t M, int64_t N, int64_t K,
                int64_t kp, float alpha, float beta, float *C, int64_t ldc, int64_t c_bstride, int batch, int b_div,
-               int lower, cudaStream_t s);
+               int lower, int kmode, cudaStream_t s);
 
 }  // namespace tc
 }  // namespace hif4x
