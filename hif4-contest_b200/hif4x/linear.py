@@ -352,6 +352,10 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
 def refine_act_values(x, values, unit, gw, gwf) -> torch.Tensor:
     """_refine_act_values (solution.py:621-663)."""
     v4, d = la.refine_prep(values, unit)
+    # M = (v4 d) @ gw - x @ gwf as the reference forms it, on round-to-nearest
+    # fp32 FMAs: the greedy flips below follow M's exact values, and moving
+    # this difference to the tensor cores (even as residual products) shifted
+    # the small-T refinements by more than a percent of output MSE
     M = la.gemm(la.mul(v4, d), gw, exact=True)
     la.gemm(x, gwf, alpha=-1.0, beta=1.0, out=M, exact=True)
     T = values.shape[0]
