@@ -346,7 +346,7 @@ def run_layer(args, rank, ws, local_rank):
     value = matrices/s over all ranks (fixed total work: strong scaling)."""
     import torch
 
-    from hif4x import linear, shard, synth
+    from hif4x import linear, shard, synth, weightset
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     dist = None
@@ -384,12 +384,20 @@ def run_layer(args, rank, ws, local_rank):
     packed = {}
 
     def step(device_resident: bool):
-        src_in, src_w = (dev_inputs, dev_weights) if device_resident else (inputs, weights)
-        for j in mine:
-            calib, test = src_in[(j.layer, j.input_id)]
-            wq, wsc = src_w[j.key]
-            res = linear.calibrate_weight(wq, wsc, calib, return_device=device_resident)
-            linear.dynamic_activation(test[0], test[1], res["activation_state"], return_device=device_resident)
+        if device_resident:
+            # independent matrices concurrently on `workers` streams
+            # longest first (the cost model), so the long matrices do not finish last
+            order = sorted(mine, key=lambda j: -shard.matrix_cost(j.N, j.C, T_cal))
+            todo = [(j.key, dev_weights[j.key], dev_inputs[(j.layer, j.input_id)][0],
+                     dev_inputs[(j.layer, j.input_id)][1]) for j in order]
+            for key, (res, _) in weightset.convert(todo, workers=args.workers, device=dev).items():
+                packed[key] = shard.pack_params(res["weight_params"])
+            return
+        for j in mine:   # the six-function API, one matrix after another, CPU tensors
+            calib, test = inputs[(j.layer, j.input_id)]
+            wq, wsc = weights[j.key]
+            res = linear.calibrate_weight(wq, wsc, calib)
+            linear.dynamic_activation(test[0], test[1], res["activation_state"])
             packed[j.key] = shard.pack_params(res["weight_params"])
 
     def barrier():
@@ -436,7 +444,8 @@ def run_layer(args, rank, ws, local_rank):
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.layers} Llama-3-8B-shaped decoder layer(s), {len(jobs)} matrices, "
                                f"{T_cal} calibration tokens per input ({n_cal} x {T_cal // n_cal}), 1 x {T_test} "
-                               "dynamic tokens per matrix", "parallelism": f"LPT over {ws} GPU(s)"},
+                               "dynamic tokens per matrix",
+                   "parallelism": f"LPT over {ws} GPU(s), {args.workers} concurrent matrices per GPU"},
         "weight_gelem_per_s": elems / dt / 1e9, "gather_s": gather_s,
         "e2e": {"value": len(jobs) / dt_api, "unit": "matrices/s", "ms_per_step": dt_api * 1e3,
                 "note": "through the six-function API: CPU tensors in, CPU dict5 and CPU states out"},
@@ -543,6 +552,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention"])
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
+    ap.add_argument("--workers", type=int, default=3, help="layer workload: matrices in flight per GPU")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "codec":
         args.warmup = 3

@@ -91,8 +91,9 @@ _SIDE: dict = {}
 
 
 def _side_stream(dev) -> torch.cuda.Stream:
-    """A second stream per device for independent calibration branches."""
-    key = str(dev)
+    """A second stream for independent calibration branches, one per
+    (device, main stream), so concurrent calibrations keep theirs apart."""
+    key = (str(dev), torch.cuda.current_stream(dev).cuda_stream)
     if key not in _SIDE:
         _SIDE[key] = torch.cuda.Stream(device=dev)
     return _SIDE[key]
@@ -119,9 +120,9 @@ def _act_factor_finish(spec, stream):
     return Ua, order
 
 
-def _randperm(n: int, k: int, dev) -> torch.Tensor:
+def _randperm(n: int, k: int, dev, rng: torch.Generator | None = None) -> torch.Tensor:
     """torch.randperm(n)[:k] on the host generator (the reference's RNG call)."""
-    return torch.randperm(n)[:min(n, k)].to(dev)
+    return torch.randperm(n, generator=rng)[:min(n, k)].to(dev)
 
 
 def _resid(x: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
@@ -171,12 +172,17 @@ def _refine_weight_values(w_final, q_used, weight_params: Dict5, calib_sm, mode)
 
 
 def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, calib_activation_list: list,
-                     info: dict | None = None, return_device: bool = False) -> dict[str, Any]:
+                     info: dict | None = None, return_device: bool = False,
+                     rng: torch.Generator | None = None) -> dict[str, Any]:
     """hif4_calibration_and_quantize_weight (solution.py:826-1026).
 
     return_device=True keeps the weight parameters and the state tensors on the
-    GPU (for device-resident pipelines); the API form returns CPU tensors."""
-    torch.manual_seed(0)                                       # solution.py:838
+    GPU (for device-resident pipelines); the API form returns CPU tensors.
+    rng: a CPU generator seeded 0 to draw the subsampling permutations from
+    instead of re-seeding the global one (the same values; lets calibrations
+    run concurrently from several threads)."""
+    if rng is None:
+        torch.manual_seed(0)                                   # solution.py:838
     dev = _dev()
     ph = _Phases(info is not None)
     ph.mark("start")
@@ -195,7 +201,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         if a_big is None or a.shape[0] > a_big.shape[0]:
             a_big = a
     logm = la.smooth_logm(abs_sum, n_tok)
-    rows = _randperm(R, 256, dev)                              # solution.py:858
+    rows = _randperm(R, 256, dev, rng)                         # solution.py:858
     w_rows = la.gather_rows(w, rows)
     best_alpha, best_loss = 0.0, None
     for alpha in ALPHA_GRID:
@@ -213,9 +219,9 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     # ---- transform choice {0: none, 1: rotation} (solution.py:875-911)
     mode, Uw, xh_pick = 0, None, None
     if R > 64 and len(acts_s) >= 2 and acts_s[-1].shape[0] >= 8:
-        rsub = _randperm(R, 256, dev)
+        rsub = _randperm(R, 256, dev, rng)
         xh_last = acts_s[-1]
-        sub = _randperm(xh_last.shape[0], 128, dev)
+        sub = _randperm(xh_last.shape[0], 128, dev, rng)
         xh_sub = la.gather_rows(xh_last, sub)
         w_sub = la.gather_rows(w_s, rsub)
         # the two spaces are independent: each runs its Hessian, Cholesky-inverse

@@ -1,0 +1,82 @@
+"""Converting many matrices on one GPU.
+
+The calibrations of independent matrices run concurrently from a few host
+threads, each on its own CUDA stream, so the latency-bound phases of one
+matrix (the 128-row Cholesky leaves, GPTQ column sweeps, small products)
+overlap with the work of another.  Each calibration draws its subsampling
+permutations from its own generator seeded 0, which gives the values the
+reference draws after torch.manual_seed(0) (solution.py:838, 858, 880-882).
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import linear
+
+
+_STREAMS: dict = {}
+
+
+def _worker_stream(dev, i: int) -> torch.cuda.Stream:
+    """Worker i's stream on `dev`, created once: the caching allocator keeps
+    memory per stream, so fresh streams on every call would re-allocate."""
+    key = (str(dev), i)
+    if key not in _STREAMS:
+        _STREAMS[key] = torch.cuda.Stream(device=dev)
+    return _STREAMS[key]
+
+
+def convert(jobs: list, workers: int = 2, device=None) -> dict:
+    """jobs: [(key, weight_pair, calib_pairs, test_pair or None)], pairs as
+    the six-function API takes them (CPU or CUDA tensors).  Returns
+    {key: (calibration result, dynamic result or None)} with every tensor left
+    on the GPU.  Work is taken from the list in order by `workers` threads, so
+    list the longest matrices first (shard.matrix_cost)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    out: dict = {}
+    errors: list = []
+    lock = threading.Lock()
+    nxt = [0]
+
+    def work(i: int):
+        torch.cuda.set_device(dev)
+        stream = _worker_stream(dev, i)
+        with torch.cuda.stream(stream):
+            while True:
+                with lock:
+                    if errors or nxt[0] >= len(jobs):
+                        break
+                    key, wpair, calib, test = jobs[nxt[0]]
+                    nxt[0] += 1
+                try:
+                    res = linear.calibrate_weight(wpair[0], wpair[1], calib, return_device=True,
+                                                  rng=torch.Generator().manual_seed(0))
+                    dyn = None
+                    if test is not None:
+                        dyn = linear.dynamic_activation(test[0], test[1], res["activation_state"],
+                                                        return_device=True)
+                    with lock:
+                        out[key] = (res, dyn)
+                except Exception as e:  # re-raised in the caller
+                    with lock:
+                        errors.append(e)
+                    break
+        stream.synchronize()
+
+    workers = max(1, min(workers, len(jobs)))
+    for i in range(workers):   # order every worker after the caller's pending work (its inputs)
+        _worker_stream(dev, i).wait_stream(torch.cuda.current_stream(dev))
+    if workers == 1:
+        work(0)
+    else:
+        ts = [threading.Thread(target=work, args=(i,)) for i in range(workers)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+    if errors:
+        raise errors[0]
+    # results produced on the workers' streams are complete (each synchronised)
+    return out

@@ -1,0 +1,41 @@
+"""Concurrent conversion of several matrices on one GPU (hif4x.weightset):
+two host threads on their own streams must give exactly the results of one
+calibration after another (every kernel is deterministic and each
+calibration draws its permutations from its own generator seeded 0)."""
+import sys
+
+import pytest
+import torch
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+sys.path.insert(0, GOLDEN)
+import pipeline_cases as pc  # noqa: E402
+
+from hif4x import linear, weightset  # noqa: E402
+
+
+def _dev(pair):
+    return [t.cuda() for t in pair]
+
+
+def test_concurrent_matches_sequential():
+    names = ["lin_c1024", "lin_c2560", "lin_c4224"]
+    jobs = []
+    for name in names:
+        wpair, calib, tests, _ = pc.linear_inputs(name)
+        jobs.append((name, _dev(wpair), [_dev(c) for c in calib], _dev(tests[0])))
+    got = weightset.convert(jobs, workers=2)
+    assert sorted(got) == sorted(names)
+    for key, wpair, calib, test in jobs:
+        ref = linear.calibrate_weight(wpair[0], wpair[1], calib, return_device=True)
+        res, dyn = got[key]
+        for k in ref["weight_params"]:
+            assert torch.equal(res["weight_params"][k], ref["weight_params"][k]), (key, k)
+        for k in ("mode", "g", "tmax"):
+            assert res["activation_state"][k] == ref["activation_state"][k], (key, k)
+        assert torch.equal(res["activation_state"]["s"], ref["activation_state"]["s"])
+        dref = linear.dynamic_activation(test[0], test[1], ref["activation_state"], return_device=True)
+        for k in ("sf", "lv2", "lv3", "sign", "mant"):
+            assert torch.equal(getattr(dyn, k), getattr(dref, k)), (key, k)
