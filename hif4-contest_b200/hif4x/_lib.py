@@ -16,7 +16,7 @@ SO_PATH = os.path.join(_HERE, "libhif4x.so")
 
 OK, NOT_PD, TIMEOUT = 0, 1, 2
 ERR_ARG, ERR_LAUNCH, ERR_UNSUPPORTED, ERR_SCRATCH = -1, -2, -3, -4
-DT_F32, DT_BF16 = 0, 1
+DT_F32, DT_BF16, DT_F64 = 0, 1, 2
 SRC_NVFP4_PACKED, SRC_NVFP4_PAIR, SRC_VALUES = 0, 1, 2
 SMOOTH_NONE, SMOOTH_MUL, SMOOTH_DIV = 0, 1, 2
 ENC_NONE, ENC_SEARCH, ENC_FAST, ENC_ALG1 = 0, 1, 2, 3
@@ -87,6 +87,13 @@ SIGNATURES: dict[str, list] = {
     "hif4x_gemm_tc": [i32, i32, i64, i64, i64, f32, vp, i64, vp, i64, f32, vp, i64, vp],
     "hif4x_device_status": [vp],
     "hif4x_gemm_simt": [i32, i32, i64, i64, i64, f32, vp, i64, i64, vp, i64, i64, f32, vp, i64, i64, i64, vp],
+    "hif4x_gemm_f64": [i32, i32, i32, i32, i64, i64, i64, ctypes.c_double, vp, i64, i64, vp, i64, i64,
+                       ctypes.c_double, vp, i64, i64, i64, i32, vp],
+    "hif4x_mirror_lower_f64": [vp, i64, i64, vp],
+    "hif4x_chol_solve_f64": [vp, i64, i64, ctypes.c_double, vp, i64, vp, vp, vp, vp],
+    "hif4x_softmax_rows": [vp, i64, i64, f32, vp],
+    "hif4x_transpose_batched": [vp, i64, i64, i64, i64, i64, vp, i64, i64, vp],
+    "hif4x_f64_to_f32": [vp, i64, vp, vp],
 }
 
 _LIB = None

@@ -22,6 +22,12 @@ import torch  # noqa: E402
 from hif4x import attention as _attn  # noqa: E402
 from hif4x import linear as _linear  # noqa: E402
 
+# The q/k carry between the attention calls of one process (the reference's
+# _QKV_CARRY): a q call empties it and records, a k call records, a v call
+# compensates against it and empties it.  clear() gives a v call the
+# isolated-call behaviour of a judge that runs each call in a fresh process.
+_QKV_CARRY = _attn.CARRY
+
 
 def _require_cuda():
     if not torch.cuda.is_available():
@@ -51,12 +57,12 @@ def hif4_calibration_attention(calib_qkv_list: list, q_num_heads: int, kv_num_he
 
 def hif4_dynamic_quantize_q(q_quant, q_scale, q_num_heads, head_dim, q_state):
     _require_cuda()
-    return _attn.dynamic_qk(q_quant, q_scale, q_state, q_num_heads, head_dim)
+    return _attn.dynamic_qk(q_quant, q_scale, q_state, q_num_heads, head_dim, role="q")
 
 
 def hif4_dynamic_quantize_k(k_quant, k_scale, kv_num_heads, head_dim, k_state):
     _require_cuda()
-    return _attn.dynamic_qk(k_quant, k_scale, k_state, kv_num_heads, head_dim)
+    return _attn.dynamic_qk(k_quant, k_scale, k_state, kv_num_heads, head_dim, role="k")
 
 
 def hif4_dynamic_quantize_v(v_quant, v_scale, kv_num_heads, head_dim, v_state):

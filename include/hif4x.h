@@ -47,6 +47,7 @@ extern "C" {
 /* ---- enums ------------------------------------------------------------- */
 #define HIF4X_DT_F32 0
 #define HIF4X_DT_BF16 1
+#define HIF4X_DT_F64 2             /* vcomp entry points only                */
 
 #define HIF4X_SRC_NVFP4_PACKED 0  /* src = codes, src_scale = e4m3, s_dec     */
 #define HIF4X_SRC_NVFP4_PAIR 1    /* src = carrier, src_scale = scale         */
@@ -276,6 +277,38 @@ int hif4x_attention(const float *Q, const float *K, const float *V, int64_t T, i
 /* (T, H, D) -> (H, T, D) (inverse = 0) or back (inverse = 1); the head
  * permutes of solution.py:1217-1225, 1353-1361. */
 int hif4x_heads_transpose(const float *in, int64_t T, int64_t H, int64_t D, int inverse, float *out, void *stream);
+
+/* ---- attention V compensation (csrc/vcomp.cu) --------------------------- */
+
+/* f64 GEMM for _v_compensate's Grams and products (example/solution/
+ * solution.py:1306-1319, torch .double() matmuls): C = alpha op(A) op(B) +
+ * beta C with A, B fp32 or f64 (a_dtype / b_dtype: HIF4X_DT_F32 or
+ * HIF4X_DT_F64), f64 accumulation and C; batched by element strides sA, sB,
+ * sC.  lower = 1 (M == N) computes only the 64 x 64 tiles on or below the
+ * diagonal. */
+int hif4x_gemm_f64(int ta, int tb, int a_dtype, int b_dtype, int64_t M, int64_t N, int64_t K, double alpha,
+                   const void *A, int64_t lda, int64_t sA, const void *B, int64_t ldb, int64_t sB, double beta,
+                   double *C, int64_t ldc, int64_t sC, int64_t batch, int lower, void *stream);
+/* Copy the lower triangle of each n x n f64 matrix onto its upper one. */
+int hif4x_mirror_lower_f64(double *A, int64_t n, int64_t batch, void *stream);
+/* torch.linalg.solve(G + lam, Cm) V of solution.py:1316-1319, as
+ * X = (A + lam 1 1^T)^-1 Rhs with lam = lam_rel * mean(diag A) added to every
+ * entry (the reference's broadcast), by a blocked f64 Cholesky and two
+ * triangular solves.  A (batch, n, n) f64, lower triangle read, overwritten;
+ * Rhs, X (batch, n, m) f64.  work: batch * (n*n + ceil(n/64)*4096 + 2*n*m)
+ * doubles; info_dev: one int.  Synchronises the stream; HIF4X_NOT_PD where a
+ * pivot is not positive (the reference's solve raising takes its fallback). */
+int hif4x_chol_solve_f64(double *A, int64_t n, int64_t batch, double lam_rel, const double *Rhs, int64_t m,
+                         double *X, double *work, int *info_dev, void *stream);
+/* torch.softmax(S / div, dim=-1) in place, fp32, rows x cols (solution.py:
+ * 1308-1311). */
+int hif4x_softmax_rows(float *S, int64_t rows, int64_t cols, float div, void *stream);
+/* out[b*obs + j*old + i] = in[b*ibs + i*ild + j], i < R, j < Cc: the
+ * (T, kvh, dh) <-> (kvh, dh, T) permutes of solution.py:1324-1330. */
+int hif4x_transpose_batched(const float *in, int64_t R, int64_t Cc, int64_t batch, int64_t ild, int64_t ibs,
+                            float *out, int64_t old, int64_t obs, void *stream);
+/* fp32 round-to-nearest of f64 (G.float(), solution.py:1327). */
+int hif4x_f64_to_f32(const double *in, int64_t n, float *out, void *stream);
 
 #ifdef __cplusplus
 }

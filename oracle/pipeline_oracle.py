@@ -10,6 +10,8 @@ rate, not bit for bit.
   upper_cholesky_inv example/solution/solution.py:287-300
   refine_rounds      example/solution/solution.py:474-521 (_rounds_np, one row
                      at a time; rows are independent)
+  vcomp_target       example/solution/solution.py:1288-1323 (_v_compensate up to
+                     the clamped target V*, before its encode and GPTQ)
 """
 from __future__ import annotations
 
@@ -86,3 +88,41 @@ def refine_rounds(M: np.ndarray, v4: np.ndarray, d: np.ndarray, G: np.ndarray, r
             M[r] += (dr * d[r, idx]) * G[idx]
             flips[r] += 1
     return M, v4, flips
+
+
+def _softmax_rows(s: np.ndarray) -> np.ndarray:
+    s = s - s.max(axis=-1, keepdims=True)
+    e = np.exp(s)
+    return (e / e.sum(axis=-1, keepdims=True)).astype(F)
+
+
+def vcomp_target(v, q_in, q_hat, k_in, k_hat, kvh: int, dh: int):
+    """(V*, G, dn): the compensated V target of _v_compensate, float64 Grams
+    and solve as the reference forms them (G + lam with lam broadcast to every
+    entry, B = (G + lam)^-1 Cm, V* = B V), then the 0.5 relative-norm clamp.
+    G is returned for the GPTQ Hessian."""
+    v, q_in, q_hat, k_in, k_hat = (np.asarray(a, F) for a in (v, q_in, q_hat, k_in, k_hat))
+    T, C = v.shape
+    qh = q_in.shape[1] // dh
+    rep = qh // kvh
+    sc = F(np.sqrt(np.float32(dh)))
+    G = np.zeros((kvh, T, T))
+    Cm = np.zeros((kvh, T, T))
+    for h in range(qh):
+        g = h // rep
+        qs, qhs = q_in[:, h * dh:(h + 1) * dh], q_hat[:, h * dh:(h + 1) * dh]
+        ks, khs = k_in[:, g * dh:(g + 1) * dh], k_hat[:, g * dh:(g + 1) * dh]
+        P = _softmax_rows((qs @ ks.T) / sc).astype(np.float64)
+        Ph = _softmax_rows((qhs @ khs.T) / sc).astype(np.float64)
+        G[g] += Ph.T @ Ph
+        Cm[g] += Ph.T @ P
+    lam = 1e-4 * np.einsum("bii->b", G) / T
+    vs = np.empty((T, C), F)
+    for g in range(kvh):
+        B = np.linalg.solve(G[g] + lam[g], Cm[g])
+        vs[:, g * dh:(g + 1) * dh] = (B @ v[:, g * dh:(g + 1) * dh].astype(np.float64)).astype(F)
+    dv = vs - v
+    dn = float(np.linalg.norm(dv.astype(np.float64)) / max(np.linalg.norm(v.astype(np.float64)), 1e-12))
+    if dn > 0.5:
+        vs = (v + dv * F(0.5 / dn)).astype(F)
+    return vs, G, dn
