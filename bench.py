@@ -346,7 +346,7 @@ def run_layer(args, rank, ws, local_rank):
     value = matrices/s over all ranks (fixed total work: strong scaling)."""
     import torch
 
-    from hif4x import linear, shard, synth, weightset
+    from hif4x import linear, score, shard, synth, weightset
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     dist = None
@@ -377,11 +377,13 @@ def run_layer(args, rank, ws, local_rank):
                             * 0.02).to(torch.bfloat16)) for j in mine}
     # device-resident copies of the same inputs
     to_dev = lambda pr: [t.to(dev) for t in pr]  # noqa: E731
+    dev_x = score.decode_pair
     dev_inputs = {k: ([to_dev(c) for c in cal], to_dev(tst)) for k, (cal, tst) in inputs.items()}
     dev_weights = {k: to_dev(v) for k, v in weights.items()}
     torch.cuda.synchronize(dev)
 
     packed = {}
+    outputs = {}
 
     def step(device_resident: bool):
         if device_resident:
@@ -390,8 +392,9 @@ def run_layer(args, rank, ws, local_rank):
             order = sorted(mine, key=lambda j: -shard.matrix_cost(j.N, j.C, T_cal))
             todo = [(j.key, dev_weights[j.key], dev_inputs[(j.layer, j.input_id)][0],
                      dev_inputs[(j.layer, j.input_id)][1]) for j in order]
-            for key, (res, _) in weightset.convert(todo, workers=args.workers, device=dev).items():
+            for key, (res, dyn) in weightset.convert(todo, workers=args.workers, device=dev).items():
                 packed[key] = shard.pack_params(res["weight_params"])
+                outputs[key] = (res["weight_params"], dyn)
             return
         for j in mine:   # the six-function API, one matrix after another, CPU tensors
             calib, test = inputs[(j.layer, j.input_id)]
@@ -426,6 +429,24 @@ def run_layer(args, rank, ws, local_rank):
 
     dt = timed(True)
     dt_api = timed(False)
+    # contest quality of this rank's matrices (the device-resident run's
+    # outputs): output MSE of the test activations through the converted
+    # weights against the NVFP4-decoded product, and the score against the
+    # Algorithm-1 standard (hif4x.score)
+    q = torch.zeros(4, dtype=torch.float64, device=dev)   # sum rel_mse, sum score, n, max rel_mse
+    for j in mine:
+        wp, dyn = outputs[j.key]
+        sc = score.linear(dev_x(dev_inputs[(j.layer, j.input_id)][1]), dev_x(dev_weights[j.key]), score.values(dyn),
+                          score.values(wp))
+        q[0] += sc["rel_mse"]
+        q[1] += sc["score"]
+        q[2] += 1
+        q[3] = max(float(q[3]), sc["rel_mse"])
+    if dist is not None:
+        qm = q[3:].clone()
+        dist.all_reduce(q, op=dist.ReduceOp.SUM)
+        dist.all_reduce(qm, op=dist.ReduceOp.MAX)
+        q[3] = qm[0]
     if dist is not None:
         g0 = time.perf_counter()
         shards = shard.gather_shards(packed, dist, dev)
@@ -447,6 +468,10 @@ def run_layer(args, rank, ws, local_rank):
                                "dynamic tokens per matrix",
                    "parallelism": f"LPT over {ws} GPU(s), {args.workers} concurrent matrices per GPU"},
         "weight_gelem_per_s": elems / dt / 1e9, "gather_s": gather_s,
+        "quality": {"mean_rel_output_mse": float(q[0] / q[2]), "max_rel_output_mse": float(q[3]),
+                    "mean_score_vs_alg1": float(q[1] / q[2]), "matrices": int(q[2]),
+                    "note": "|X W^T - X^ W^^T|^2 / |X W^T|^2 on each matrix's 1024-token test input; "
+                            "score = (MSE_alg1 - MSE) / MSE_alg1 (the contest's rule)"},
         "e2e": {"value": len(jobs) / dt_api, "unit": "matrices/s", "ms_per_step": dt_api * 1e3,
                 "note": "through the six-function API: CPU tensors in, CPU dict5 and CPU states out"},
         "timing_note": "CUDA events on the launching stream around the timed steps, max over ranks",
@@ -465,7 +490,7 @@ def run_attention(args, rank, ws, local_rank):
     softmax(QK^T/sqrt(128))V from the converted tensors against bf16."""
     import torch
 
-    from hif4x import attention, codec, synth
+    from hif4x import attention, codec, score, synth
     from hif4x import linalg as la
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -514,6 +539,7 @@ def run_attention(args, rank, ws, local_rank):
     dt = e0.elapsed_time(e1) / 1e3 / max(args.steps, 1)
     # quality on this rank's first item: converted vs bf16 attention output
     rel = float("nan")
+    sc = {}
     if mine:
         b = mine[0]
         x = raw[b][1]
@@ -521,6 +547,7 @@ def run_attention(args, rank, ws, local_rank):
         ref = attention.attention_out(x["q"].float(), x["k"].float(), x["v"].float(), qh, kvh, dh)
         got = attention.attention_out(codec.decode(pq), codec.decode(pk), codec.decode(pv), qh, kvh, dh)
         rel = la.mse(got, ref) / max(la.mse(ref), 1e-30)
+        sc = score.attention_case(nv[b][1], pq, pk, pv, qh, kvh, dh)
     if dist is not None:
         t = torch.tensor([dt], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -537,7 +564,8 @@ def run_attention(args, rank, ws, local_rank):
                                f"bf16 NVFP4, GQA {qh // kvh}:1, K RoPE-paired with 4 outlier pairs x15; "
                                f"calibration from 1 x {T_cal}-token sample + {T}-token hold-out",
                    "parallelism": f"batch items round-robin over {ws} GPU(s)"},
-        "quality": {"rel_err_softmax_qkv": rel, "item": mine[0] if mine else None},
+        "quality": {"rel_err_softmax_qkv": rel, "item": mine[0] if mine else None,
+                    "rel_output_mse_vs_nvfp4": sc.get("rel_mse"), "score_vs_alg1": sc.get("score")},
         "timing_note": "CUDA events on the launching stream, max over ranks",
     }), flush=True)
 
