@@ -191,6 +191,61 @@ __global__ void axpby_kernel(const float *a, const float *b, const float *c, flo
   out[e] = v;
 }
 
+// E2M1 value -> nibble (sign<<3 | index of |v| in {0, .5, 1, 1.5, 2, 3, 4, 6});
+// -1 when v is not one of the 16 values (NaN and infinities included).
+__device__ __forceinline__ int e2m1_nibble(float v) {
+  const float a = fabsf(v);
+  int idx;
+  if (a == 0.0f) idx = 0;
+  else if (a == 0.5f) idx = 1;
+  else if (a == 1.0f) idx = 2;
+  else if (a == 1.5f) idx = 3;
+  else if (a == 2.0f) idx = 4;
+  else if (a == 3.0f) idx = 5;
+  else if (a == 4.0f) idx = 6;
+  else if (a == 6.0f) idx = 7;
+  else return -1;
+  return idx | (signbit(v) ? 8 : 0);
+}
+
+// Pack an NVFP4 carrier (fp32 or bf16 E2M1 values, n even) two elements per
+// byte, element 2i in the low nibble; counts the elements that are not E2M1
+// values (their nibble is written as 0).
+__global__ void e2m1_pack_kernel(const void *carrier, int dtype, int64_t npair, uint8_t *codes, int *bad) {
+  const int64_t i = (int64_t)blockIdx.x * UT + threadIdx.x;
+  if (i >= npair) return;
+  float v0, v1;
+  if (dtype == HIF4X_DT_BF16) {
+    const uint32_t w = ((const uint32_t *)carrier)[i];
+    v0 = __uint_as_float(w << 16);
+    v1 = __uint_as_float(w & 0xffff0000u);
+  } else {
+    const float2 w = ((const float2 *)carrier)[i];
+    v0 = w.x;
+    v1 = w.y;
+  }
+  int n0 = e2m1_nibble(v0), n1 = e2m1_nibble(v1);
+  if (n0 < 0 || n1 < 0) {
+    atomicAdd(bad, 1);
+    n0 = n0 < 0 ? 0 : n0;
+    n1 = n1 < 0 ? 0 : n1;
+  }
+  codes[i] = (uint8_t)(n0 | (n1 << 4));
+}
+
+// Inverse of e2m1_pack_kernel: codes -> bf16 or fp32 carrier (-0 kept).
+__global__ void e2m1_unpack_kernel(const uint8_t *codes, int64_t npair, void *carrier, int dtype) {
+  const int64_t i = (int64_t)blockIdx.x * UT + threadIdx.x;
+  if (i >= npair) return;
+  const uint32_t b = codes[i];
+  const float v0 = e2m1_to_f32(b & 15u), v1 = e2m1_to_f32(b >> 4);
+  if (dtype == HIF4X_DT_BF16) {
+    ((uint32_t *)carrier)[i] = (__float_as_uint(v0) >> 16) | (__float_as_uint(v1) & 0xffff0000u);
+  } else {
+    ((float2 *)carrier)[i] = make_float2(v0, v1);
+  }
+}
+
 }  // namespace hif4x
 
 using namespace hif4x;
@@ -330,6 +385,24 @@ extern "C" int hif4x_axpby(const float *a, const float *b, const float *c, float
   if (n == 0) return HIF4X_OK;
   if (!a || !out) return HIF4X_ERR_ARG;
   axpby_kernel<<<nb_(n), UT, 0, (cudaStream_t)stream>>>(a, b, c, alpha, n, out);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_e2m1_pack(const void *carrier, int dtype, int64_t n, uint8_t *codes, int *bad_dev, void *stream) {
+  if (n < 0 || (n & 1) || (dtype != HIF4X_DT_F32 && dtype != HIF4X_DT_BF16)) return HIF4X_ERR_ARG;
+  if (n == 0) return HIF4X_OK;
+  if (!carrier || !codes || !bad_dev) return HIF4X_ERR_ARG;
+  e2m1_pack_kernel<<<nb_(n / 2), UT, 0, (cudaStream_t)stream>>>(carrier, dtype, n / 2, codes, bad_dev);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_e2m1_unpack(const uint8_t *codes, int64_t n, void *carrier, int dtype, void *stream) {
+  if (n < 0 || (n & 1) || (dtype != HIF4X_DT_F32 && dtype != HIF4X_DT_BF16)) return HIF4X_ERR_ARG;
+  if (n == 0) return HIF4X_OK;
+  if (!carrier || !codes) return HIF4X_ERR_ARG;
+  e2m1_unpack_kernel<<<nb_(n / 2), UT, 0, (cudaStream_t)stream>>>(codes, n / 2, carrier, dtype);
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
 }

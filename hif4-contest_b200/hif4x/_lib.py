@@ -94,6 +94,8 @@ SIGNATURES: dict[str, list] = {
     "hif4x_softmax_rows": [vp, i64, i64, f32, vp],
     "hif4x_transpose_batched": [vp, i64, i64, i64, i64, i64, vp, i64, i64, vp],
     "hif4x_f64_to_f32": [vp, i64, vp, vp],
+    "hif4x_e2m1_pack": [vp, i32, i64, vp, vp, vp],
+    "hif4x_e2m1_unpack": [vp, i64, vp, i32, vp],
 }
 
 _LIB = None

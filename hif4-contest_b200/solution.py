@@ -34,11 +34,19 @@ def _require_cuda():
         raise RuntimeError("hif4x solution needs a CUDA device (B200, sm_100a)")
 
 
+# HIF4X_COMPACT_STATE=1: the calibration writes the compact activation state
+# (packed weight values and NVFP4 weight, ~6x smaller than the reference's
+# C x C u_act / gw / gwf at C = 4096); the dynamic call rebuilds those on the
+# GPU and returns the same parameters.  Off by default: the state then has
+# the reference's keys and tensors.
+_COMPACT = os.environ.get("HIF4X_COMPACT_STATE", "0") == "1"
+
+
 def hif4_calibration_and_quantize_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor,
                                          calib_activation_list: list) -> dict[str, Any]:
     """Weight HiF4 parameters + activation_state (solution.py:826-1026)."""
     _require_cuda()
-    return _linear.calibrate_weight(weight_quant, weight_scale, calib_activation_list)
+    return _linear.calibrate_weight(weight_quant, weight_scale, calib_activation_list, compact=_COMPACT)
 
 
 def hif4_dynamic_quantize_activation(activation_quant: torch.Tensor, activation_scale: torch.Tensor,

@@ -266,6 +266,15 @@ int hif4x_refine_prep(const float *values, const float *unit, int64_t n, float *
 /* out = a*b + alpha*c elementwise (b, c may be NULL). */
 int hif4x_axpby(const float *a, const float *b, const float *c, float alpha, int64_t n, float *out, void *stream);
 
+/* Compact activation state (no counterpart in the reference, which carries
+ * u_act / gw / gwf as C x C tensors, solution.py:1016-1025): an NVFP4
+ * carrier of E2M1 values (fp32 or bf16, n even) packed two per byte, element
+ * 2i in the low nibble, nibble = sign<<3 | E2M1 index (-0 kept); *bad_dev
+ * (device int, not cleared here) counts elements that are not E2M1 values. */
+int hif4x_e2m1_pack(const void *carrier, int dtype, int64_t n, uint8_t *codes, int *bad_dev, void *stream);
+/* Inverse of hif4x_e2m1_pack into a bf16 or fp32 carrier. */
+int hif4x_e2m1_unpack(const uint8_t *codes, int64_t n, void *carrier, int dtype, void *stream);
+
 /* ---- attention path (csrc/attention.cu) -------------------------------- */
 
 /* _attention_out / attn_ref (example/solution/solution.py:1247-1258,
