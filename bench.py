@@ -399,7 +399,7 @@ def run_layer(args, rank, ws, local_rank):
         for j in mine:   # the six-function API, one matrix after another, CPU tensors
             calib, test = inputs[(j.layer, j.input_id)]
             wq, wsc = weights[j.key]
-            res = linear.calibrate_weight(wq, wsc, calib)
+            res = linear.calibrate_weight(wq, wsc, calib, compact=compact_api)
             linear.dynamic_activation(test[0], test[1], res["activation_state"])
             packed[j.key] = shard.pack_params(res["weight_params"])
 
@@ -427,8 +427,11 @@ def run_layer(args, rank, ws, local_rank):
             dt = float(t[0])
         return dt
 
+    compact_api = False
     dt = timed(True)
     dt_api = timed(False)
+    compact_api = True
+    dt_api_compact = timed(False)
     # contest quality of this rank's matrices (the device-resident run's
     # outputs): output MSE of the test activations through the converted
     # weights against the NVFP4-decoded product, and the score against the
@@ -473,7 +476,9 @@ def run_layer(args, rank, ws, local_rank):
                     "note": "|X W^T - X^ W^^T|^2 / |X W^T|^2 on each matrix's 1024-token test input; "
                             "score = (MSE_alg1 - MSE) / MSE_alg1 (the contest's rule)"},
         "e2e": {"value": len(jobs) / dt_api, "unit": "matrices/s", "ms_per_step": dt_api * 1e3,
-                "note": "through the six-function API: CPU tensors in, CPU dict5 and CPU states out"},
+                "note": "through the six-function API: CPU tensors in, CPU dict5 and CPU states out",
+                "compact_state": {"value": len(jobs) / dt_api_compact, "unit": "matrices/s",
+                                  "ms_per_step": dt_api_compact * 1e3}},
         "timing_note": "CUDA events on the launching stream around the timed steps, max over ranks",
     }), flush=True)
 

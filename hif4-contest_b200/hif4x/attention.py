@@ -14,6 +14,7 @@ import torch
 
 from . import _lib as L
 from . import codec
+from . import hostio
 from . import linalg as la
 from . import vcomp
 from .linear import _dev, decode_pair
@@ -168,8 +169,8 @@ def calibrate(calib_qkv_list: list, q_num_heads: int, kv_num_heads: int, head_di
     q_state = {"rot": rot, "kvh": kvh}
     k_state = {"rot": rot, "kvh": kvh}
     if gq == 1:
-        q_state.update({"gq": 1, "u": Uq.cpu().contiguous()})
-        k_state.update({"gq": 1, "u": Uk.cpu().contiguous()})
+        q_state.update({"gq": 1, "u": hostio.to_host(Uq)})
+        k_state.update({"gq": 1, "u": hostio.to_host(Uk)})
     return {"q_state": q_state, "k_state": k_state, "v_state": None}
 
 
@@ -191,7 +192,7 @@ def dynamic_qk(quant, scale, state, num_heads: int, head_dim: int, role: str | N
         kvh_n = state.get("kvh")
         if isinstance(u, torch.Tensor) and isinstance(kvh_n, int) and num_heads % kvh_n == 0:
             rep_n = num_heads // kvh_n
-            u = u.float().to(dev).contiguous()
+            u = hostio.to_device(u, dev).float().contiguous()
             u_full = u[:num_heads].contiguous() if num_heads <= u.shape[0] else _u_by_head(u, num_heads, rep_n)
             qs = la.gptq(heads_first(x, num_heads), heads_first(unit, num_heads), u_full)
             values = heads_last(qs)

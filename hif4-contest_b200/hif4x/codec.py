@@ -14,6 +14,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
+from . import hostio
 
 GROUP = 64
 
@@ -42,7 +43,7 @@ class Dict5:
         """The reference's dict5 (example/self_check.py:75-95 shapes)."""
         R, C = self.sign.shape
         nb = C // GROUP
-        t = (lambda x: x.cpu()) if cpu else (lambda x: x)
+        t = hostio.to_host if cpu else (lambda x: x)
         return {"scale_factor": t(self.sf).reshape(R, nb, 1, 1, 1),
                 "scale_lv2": t(self.lv2).reshape(R, nb, 8, 1, 1),
                 "scale_lv3": t(self.lv3).reshape(R, nb, 8, 2, 1),

@@ -15,6 +15,7 @@ import torch
 
 from . import _lib as L
 from . import codec
+from . import hostio
 from . import linalg as la
 from .codec import Dict5
 
@@ -33,8 +34,8 @@ def _dev():
 
 def upload_pair(pair, dev) -> tuple[torch.Tensor, torch.Tensor]:
     q, s = pair
-    q = q.to(dev, non_blocking=True)
-    s = s.to(dev, non_blocking=True)
+    q = hostio.to_device(q, dev)
+    s = hostio.to_device(s, dev)
     if q.dtype not in (torch.float32, torch.bfloat16):
         q = q.float()
     if s.dtype not in (torch.float32, torch.bfloat16):
@@ -344,7 +345,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         info.update(alpha=best_alpha, mode=mode, gptq_w=gptq_w, gptq_act=gptq_act, e3=refined, tmax=tmax,
                     w_final=w_final, q_used=q_used, s=s)
     la.check_device_status(dev)
-    out = (lambda t: t) if return_device else (lambda t: t.cpu().contiguous())
+    out = (lambda t: t) if return_device else hostio.to_host
     activation_state = {
         "s": out(s),
         "mode": mode,
@@ -419,8 +420,8 @@ def compact_state(wp_act, wp_final, weight_quant, weight_scale, *, need_ua: bool
 
 
 def _unpack_values(meta: torch.Tensor, codes: torch.Tensor, dev) -> torch.Tensor:
-    m = meta.to(dev).contiguous()
-    c = codes.to(dev).contiguous().view(torch.uint8)
+    m = hostio.to_device(meta, dev)
+    c = hostio.to_device(codes, dev).view(torch.uint8)
     return codec.decode(codec.unpack(m, c))
 
 
@@ -449,7 +450,7 @@ def _rebuild(st: dict, C: int, dev, need_ua: bool, need_grams: bool):
         gw = la.to_bf16(Hf if Hf is not None else la.gram(qf))
         N = wc.shape[0]
         carrier = torch.empty(N, C, dtype=torch.bfloat16 if st.get("w_bf16") else torch.float32, device=dev)
-        L.call("hif4x_e2m1_unpack", L.ptr(wc.to(dev).contiguous()), N * C, L.ptr(carrier),
+        L.call("hif4x_e2m1_unpack", L.ptr(hostio.to_device(wc, dev)), N * C, L.ptr(carrier),
                L.dtype_code(carrier.dtype), L.stream(dev))
         w = decode_pair((carrier, wsc), dev)
         s = st.get("s")
@@ -511,7 +512,7 @@ def dynamic_activation(activation_quant: torch.Tensor, activation_scale: torch.T
         u = st.get("u_act")
         order = st.get("order")
         if isinstance(u, torch.Tensor) and tuple(u.shape) == (C, C):
-            u = u.float().to(dev).contiguous()
+            u = hostio.to_device(u, dev).float().contiguous()
             if isinstance(order, torch.Tensor) and order.numel() == C:
                 ol = order.long().to(dev)
                 values = la.scatter_cols(la.gptq(la.gather_cols(x, ol), la.gather_cols(unit, ol), u), ol)
@@ -524,8 +525,8 @@ def dynamic_activation(activation_quant: torch.Tensor, activation_scale: torch.T
                 and tuple(gw.shape) == (C, C) and tuple(gwf.shape) == (C, C)):
             try:
                 v0 = values if values is not None else codec.decode(p)
-                v1 = refine_act_values(x, v0, unit, la.to_f32(gw.to(dev).contiguous()),
-                                       la.to_f32(gwf.to(dev).contiguous()))
+                v1 = refine_act_values(x, v0, unit, la.to_f32(hostio.to_device(gw, dev)),
+                                       la.to_f32(hostio.to_device(gwf, dev)))
                 result = codec.values_to_params(v1, p)
             except L.Hif4xError:
                 result = None

@@ -22,6 +22,7 @@ import torch
 
 from . import _lib as L
 from . import codec
+from . import hostio
 from . import linalg as la
 from .attention import attention_out
 from .codec import Dict5
@@ -40,11 +41,9 @@ def values(p) -> torch.Tensor:
     dev = torch.device("cuda", torch.cuda.current_device())
     sf = p["scale_factor"]
     R, nb = sf.shape[0], sf.shape[1]
-    d5 = Dict5(sf.reshape(R, nb).to(dev).float().contiguous(),
-               p["scale_lv2"].reshape(R, nb, 8).to(dev).float().contiguous(),
-               p["scale_lv3"].reshape(R, nb, 16).to(dev).float().contiguous(),
-               p["sign"].reshape(R, nb * 64).to(dev).float().contiguous(),
-               p["mant"].reshape(R, nb * 64).to(dev).float().contiguous())
+    up = lambda t, *shape: hostio.to_device(t.reshape(*shape), dev).float().contiguous()  # noqa: E731
+    d5 = Dict5(up(sf, R, nb), up(p["scale_lv2"], R, nb, 8), up(p["scale_lv3"], R, nb, 16),
+               up(p["sign"], R, nb * 64), up(p["mant"], R, nb * 64))
     return codec.decode(d5)
 
 

@@ -69,14 +69,14 @@ def rank_jobs(jobs: list[MatrixJob], rank: int, world: int, T_cal: int) -> list[
 
 def pack_params(p: dict) -> torch.Tensor:
     """dict5 (CPU, reference shapes) -> one uint8 buffer: packed HiF4 (meta + codes)."""
-    from . import codec
+    from . import codec, hostio
     sf = p["scale_factor"]
     R, nb = sf.shape[0], sf.shape[1]
     C = nb * 64
     dev = torch.device("cuda", torch.cuda.current_device())
-    d5 = codec.Dict5(sf.reshape(R, nb).to(dev).contiguous(), p["scale_lv2"].reshape(R, nb, 8).to(dev).contiguous(),
-                     p["scale_lv3"].reshape(R, nb, 16).to(dev).contiguous(),
-                     p["sign"].reshape(R, C).to(dev).contiguous(), p["mant"].reshape(R, C).to(dev).contiguous())
+    up = lambda t, *shape: hostio.to_device(t.reshape(*shape), dev)  # noqa: E731
+    d5 = codec.Dict5(up(sf, R, nb), up(p["scale_lv2"], R, nb, 8), up(p["scale_lv3"], R, nb, 16),
+                     up(p["sign"], R, C), up(p["mant"], R, C))
     meta, codes = codec.pack(d5)
     return torch.cat([meta.view(torch.uint8).reshape(-1), codes.reshape(-1)])
 
