@@ -153,6 +153,38 @@ __device__ __forceinline__ void load_group(const ConvParams &p, int64_t g, float
   }
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic, round-to-nearest per lane)
+typedef unsigned long long u64;
+__device__ __forceinline__ u64 pk2(float lo, float hi) {
+  u64 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(u64 v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
+  u64 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b) {
+  u64 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+  u64 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 sub2(u64 a, u64 b) {
+  u64 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+
 // ---------------------------------------------------------------- rotation
 // out[e] = sum_{d=0..63} x[d] * (H64[d][e] / 8 * sign_e), summed d = 0..63
 // from +0 as torch's CPU einsum does (solution.py:243-245).
@@ -190,20 +222,37 @@ __device__ __forceinline__ void rot64_exact(float (&x)[64], uint64_t sgn, float 
   }
   const bool fast = (L >= -120) && (L + 23 > 127 || S < exp2i(L + 23));
   if (fast) {
+    // stage h = 1 pairs neighbours (scalar); stages h = 2..32 run on f32x2
+    // pairs {x[2i], x[2i+1]} (the same IEEE operations lane by lane)
+    u64 P[32];
 #pragma unroll
-    for (int lg = 0; lg < 6; lg++) {
+    for (int i = 0; i < 32; i++) P[i] = pk2(__fadd_rn(x[2 * i], x[2 * i + 1]), __fsub_rn(x[2 * i], x[2 * i + 1]));
 #pragma unroll
-      for (int j = 0; j < 64; j++) {
-        const int h = 1 << lg;
-        if ((j & h) == 0) {
-          const float a = x[j], b = x[j + h];
-          x[j] = __fadd_rn(a, b);
-          x[j + h] = __fsub_rn(a, b);
+    for (int lg = 0; lg < 5; lg++) {
+      const int h = 1 << lg;   // pair distance
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        if ((i & h) == 0) {
+          const u64 a = P[i], b = P[i + h];
+          P[i] = add2(a, b);
+          P[i + h] = sub2(a, b);
         }
       }
     }
+    // x[e] * (+-1/8): the exact power-of-two scaling packed, the sign of
+    // column e flipped by xor from bit e of the column's sign word
+    const u64 EIGHTH = pk2(0.125f, 0.125f);
+    const uint32_t s_lo = (uint32_t)sgn, s_hi = (uint32_t)(sgn >> 32);
 #pragma unroll
-    for (int e = 0; e < 64; e++) x[e] = __fmul_rn(x[e], ((sgn >> e) & 1ull) ? -0.125f : 0.125f);
+    for (int i = 0; i < 32; i++) {
+      float lo, hi;
+      upk2(mul2(P[i], EIGHTH), lo, hi);
+      const int e = 2 * i;
+      const uint32_t w = e < 32 ? s_lo : s_hi;
+      const int b0 = e & 31;
+      x[e] = __uint_as_float(__float_as_uint(lo) ^ ((w << (31 - b0)) & 0x80000000u));
+      x[e + 1] = __uint_as_float(__float_as_uint(hi) ^ ((w << (30 - b0)) & 0x80000000u));
+    }
     return;
   }
   // Sequential path (wide dynamic range): the reference's order exactly.
@@ -241,32 +290,6 @@ struct Enc {
 // range, so the 6 candidates x 3 lv units collapse onto 14 distinct units
 // sig * 2^(e0+m) (sig in {1, 1.25, 1.5, 1.75}; m in 0..3 for sig 1, 1.25
 // and 0..2 for 1.5, 1.75), each evaluated once per element.
-// ---- packed fp32 pairs (sm_100 f32x2 arithmetic, round-to-nearest per lane)
-typedef unsigned long long u64;
-__device__ __forceinline__ u64 pk2(float lo, float hi) {
-  u64 r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void upk2(u64 v, float &lo, float &hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
-  u64 d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ u64 add2(u64 a, u64 b) {
-  u64 d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
-  u64 d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
 // The per-element unit work runs on f32x2 pairs; each lane is an IEEE RN fp32
 // operation, so values and order equal the scalar restatement.  Pairs
 // (sig s, scale m):
@@ -566,35 +589,46 @@ __global__ void __launch_bounds__(kConvThreads, 5) convert_kernel(const ConvPara
     enc.bits = bits;
   }
 
-  // ---- element pass, packed HiF4 only (searched encode): the mantissa code
-  // is read from the magic-number float's bits (t - 1.5*2^23 is an integer
-  // in 0..7 and t's ulp is 1).
+  // ---- element pass, packed HiF4 only (searched encode), on f32x2 pairs.
+  // m4 = min(RNE(q), 7) with q = |x| / unit * 4 is RNE(min(q, 7.25)) (RNE is
+  // monotone and 7.25 rounds to 7), so one clamp before the magic-number
+  // rounding covers every q >= 0 (infinities too); t + 1.5*2^23 then holds m4
+  // in its low three bits.
   if (PACKED_ONLY) {
     const float sf = enc.sf;
     const float ysf = __fdiv_rn(1.0f, sf);
     p.meta[g] = e6m2_code(sf) | ((enc.bits & 0xffu) << 8) | ((enc.bits >> 8) << 16);
+    const u64 YSF2 = pk2(ysf, ysf), NSF2 = pk2(-sf, -sf), MAG2 = pk2(kMagic, kMagic);
     const uint32_t magic_bits = __float_as_uint(kMagic);
 #pragma unroll 1
     for (int i = 0; i < 8; i++) {
       const uint32_t l2 = (enc.bits >> i) & 1u;
       uint32_t nib = 0;
 #pragma unroll
-      for (int k = 0; k < 8; k++) {
-        const int el = 8 * i + k;
-        const uint32_t l3 = (enc.bits >> (8 + 2 * i + k / 4)) & 1u;
-        const float a = stage[el * st];
-        const float q0 = __fmul_rn(a, ysf);
-        const float q = __fmaf_rn(__fmaf_rn(-q0, sf, a), ysf, q0);
-        const float qs = __fmul_rn(q, (l2 + l3) == 0 ? 4.0f : ((l2 + l3) == 1 ? 2.0f : 1.0f));
-        uint32_t m4;
-        if (qs < 4194304.0f) {
-          m4 = __float_as_uint(fminf(__fadd_rn(qs, kMagic), kMagic + 7.0f)) - magic_bits;
-        } else {
-          m4 = 7u;
+      for (int qd = 0; qd < 2; qd++) {
+        const uint32_t l3 = (enc.bits >> (8 + 2 * i + qd)) & 1u;
+        const float mq = exp2i(2 - (int)(l2 + l3));            // 4, 2 or 1: unit = sf * 2^(l2+l3)
+        const u64 M2 = pk2(mq, mq);
+#pragma unroll
+        for (int pr = 0; pr < 2; pr++) {
+          const int el = 8 * i + 4 * qd + 2 * pr;
+          const u64 a2 = pk2(stage[el * st], stage[(el + 1) * st]);
+          const u64 q0 = mul2(a2, YSF2);
+          const u64 q = mul2(fma2(fma2(q0, NSF2, a2), YSF2, q0), M2);   // Markstein quotient, rescaled
+          float lo, hi;
+          upk2(q, lo, hi);
+          float rl, rh;
+          upk2(add2(pk2(fminf(lo, 7.25f), fminf(hi, 7.25f)), MAG2), rl, rh);
+          const uint32_t two = (__float_as_uint(rl) - magic_bits) | ((__float_as_uint(rh) - magic_bits) << 4);
+          nib |= two << (4 * (4 * qd + 2 * pr));
         }
-        nib |= ((uint32_t)((neg >> el) & 1ull) << 3 | m4) << (4 * k);
       }
-      reinterpret_cast<uint32_t *>(p.codes)[g * 8 + i] = nib;
+      // sign bits of the sub-block to bit 3 of each nibble
+      uint32_t sb = (uint32_t)(neg >> (8 * i)) & 0xffu;
+      sb = (sb | (sb << 12)) & 0x000f000fu;
+      sb = (sb | (sb << 6)) & 0x03030303u;
+      sb = (sb | (sb << 3)) & 0x11111111u;
+      reinterpret_cast<uint32_t *>(p.codes)[g * 8 + i] = nib | (sb << 3);
     }
     return;
   }
