@@ -360,17 +360,16 @@ __device__ __forceinline__ Enc search_fast2(const float *stage, int st, int e0) 
 #pragma unroll
     for (int c = 0; c < 6; c++) {
       const int b0 = BASE[c];
-      const bool t0 = Q[0][b0] <= Q[0][b0 + 1];
-      const bool t1 = Q[1][b0] <= Q[1][b0 + 1];
-      const float e2a = __fadd_rn(t0 ? Q[0][b0] : Q[0][b0 + 1], t1 ? Q[1][b0] : Q[1][b0 + 1]);
-      const bool s0 = Q[0][b0 + 1] <= Q[0][b0 + 2];
-      const bool s1 = Q[1][b0 + 1] <= Q[1][b0 + 2];
-      const float e2b = __fadd_rn(s0 ? Q[0][b0 + 1] : Q[0][b0 + 2], s1 ? Q[1][b0 + 1] : Q[1][b0 + 2]);
+      const float a0 = Q[0][b0], a1 = Q[0][b0 + 1], a2 = Q[0][b0 + 2];
+      const float c0 = Q[1][b0], c1 = Q[1][b0 + 1], c2 = Q[1][b0 + 2];
+      // lv3 per quad: unit b0 on ties (<=); lv2: the first choice unless strictly better
+      const float e2a = __fadd_rn(fminf(a0, a1), fminf(c0, c1));
+      const float e2b = __fadd_rn(fminf(a1, a2), fminf(c1, c2));
       const bool take2 = e2b < e2a;
-      const float best = take2 ? e2b : e2a;
-      const uint32_t l3 = take2 ? ((s0 ? 0u : 1u) | (s1 ? 0u : 2u)) : ((t0 ? 0u : 1u) | (t1 ? 0u : 2u));
+      const uint32_t l3 = take2 ? ((a1 > a2 ? 1u : 0u) | (c1 > c2 ? 2u : 0u))
+                                : ((a0 > a1 ? 1u : 0u) | (c0 > c1 ? 2u : 0u));
       bits[c] |= ((take2 ? 1u : 0u) << i) | (l3 << (8 + 2 * i));
-      err[c] = __fadd_rn(err[c], best);
+      err[c] = __fadd_rn(err[c], fminf(e2a, e2b));
     }
   }
   int cb = 0;
