@@ -762,6 +762,17 @@ __global__ void __launch_bounds__(256) decode_packed_kernel(const uint32_t *__re
   }
 }
 
+// Packed HiF4 rows: row r of the output is its C/2 code bytes followed by
+// its C/64 meta words (9C/16 bytes per row), one thread per 4-byte word.
+__global__ void hif4_rows_kernel(const uint32_t *__restrict__ meta, const uint32_t *__restrict__ codes,
+                                 int64_t rows, int64_t cw, int64_t mw, uint32_t *__restrict__ out) {
+  const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t pw = cw + mw;
+  if (w >= rows * pw) return;
+  const int64_t r = w / pw, j = w - r * pw;
+  out[w] = j < cw ? __ldcs(codes + r * cw + j) : __ldcs(meta + r * mw + (j - cw));
+}
+
 // dict5 -> values, one thread per element: ((((sign*mant)*lv3)*lv2)*sf)
 __global__ void decode_dict5_kernel(const float *sf, const float *lv2, const float *lv3, const float *sign,
                                     const float *mant, int64_t n, void *out, int out_dtype) {
@@ -1041,6 +1052,19 @@ extern "C" int hif4x_unpack_dict5(const uint32_t *meta, const uint8_t *codes, in
   const int64_t ng = rows * (cols / 64);
   if (ng == 0) return HIF4X_OK;
   unpack_dict5_kernel<<<nblocks(ng, 128), 128, 0, (cudaStream_t)stream>>>(meta, codes, ng, sf, lv2, lv3, sign, mant);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_hif4_rows(const uint32_t *meta, const uint8_t *codes, int64_t rows, int64_t cols, uint8_t *out,
+                               void *stream) {
+  if (!meta || !codes || !out || rows < 0 || cols % 64 != 0 || (reinterpret_cast<uintptr_t>(codes) & 3u) ||
+      (reinterpret_cast<uintptr_t>(out) & 3u))
+    return HIF4X_ERR_ARG;
+  const int64_t cw = cols / 8, mw = cols / 64, n = rows * (cw + mw);
+  if (n == 0) return HIF4X_OK;
+  hif4_rows_kernel<<<nblocks(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      meta, reinterpret_cast<const uint32_t *>(codes), rows, cw, mw, reinterpret_cast<uint32_t *>(out));
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
 }

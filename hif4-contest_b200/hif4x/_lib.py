@@ -96,6 +96,7 @@ SIGNATURES: dict[str, list] = {
     "hif4x_f64_to_f32": [vp, i64, vp, vp],
     "hif4x_e2m1_pack": [vp, i32, i64, vp, vp, vp],
     "hif4x_e2m1_unpack": [vp, i64, vp, i32, vp],
+    "hif4x_hif4_rows": [vp, vp, i64, i64, vp, vp],
 }
 
 _LIB = None

@@ -149,6 +149,12 @@ int hif4x_values_to_params(const float *q, const float *sf, const float *lv2, co
 int hif4x_unit_flat(const float *sf, const float *lv2, const float *lv3, int64_t rows, int64_t cols,
                     float *unit, void *stream);
 
+/* Packed HiF4 rows (no counterpart in the reference, which only
+ * materialises dict5): row r of `out` is the row's C/2 code bytes followed by
+ * its C/64 meta words, 9C/16 bytes per row, so a row range of a converted
+ * tensor leaves the device in one contiguous copy.  codes, out 4-byte aligned. */
+int hif4x_hif4_rows(const uint32_t *meta, const uint8_t *codes, int64_t rows, int64_t cols, uint8_t *out,
+                    void *stream);
 /* dict5 <-> HiF4 packed.  Unpack writes sign = 0 where mant == 0 and the
  * packed sign bit is clear, -1 where it is set (the packed form keeps the
  * value, not the sign of a zero element). */
