@@ -715,6 +715,96 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_warp_kernel(float *
   }
 }
 
+// Row-exchange form for large row counts: each warp owns RW rows (RW <= 16);
+// lane l holds block columns l, l+32, l+64, l+96 of all of them.  For column
+// i the owner lane publishes its RW values through shared memory, lanes
+// 0..RW-1 quantize one row each (the warp issues the quantisation once, not
+// once per row), publish the scaled errors back, and every lane updates its
+// later columns.  Same operations in the same order as
+// gptq_block_warp_kernel, so the results are identical.
+constexpr int GQX_MAXRW = 16;
+template <int RW>
+__global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_xch_kernel(float *W, const float *unit, const float *U,
+                                                                        float *Q, float *E, int64_t R, int64_t C,
+                                                                        int64_t i1, int nb, int64_t bstride_rows,
+                                                                        int64_t bstride_u) {
+  extern __shared__ float Hs[];   // [nb][nb], then per warp [RW] column values + [RW] errors
+  const int64_t bz = blockIdx.y;
+  W += bz * bstride_rows * C;
+  unit += bz * bstride_rows * C;
+  Q += bz * bstride_rows * C;
+  E += bz * bstride_rows * GQ_BLK;
+  U += bz * bstride_u;
+  for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float *xw = Hs + GQ_BLK * GQ_BLK + warp * (2 * GQX_MAXRW);
+  float *xe = xw + GQX_MAXRW;
+  const int64_t r0 = ((int64_t)blockIdx.x * GQW_WARPS + warp) * RW;
+  if (r0 >= R) return;
+  float w[RW][4];
+#pragma unroll
+  for (int rr = 0; rr < RW; rr++) {
+    const int64_t r = r0 + rr;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int c = lane + 32 * k;
+      w[rr][k] = (r < R && c < nb) ? W[r * C + i1 + c] : 0.0f;
+    }
+  }
+  const int64_t rq = r0 + lane;             // the row this lane quantizes (lanes < RW)
+  const bool qlane = lane < RW;
+  const bool qrow = qlane && rq < R;
+  const float *urow = unit + (qrow ? rq : 0) * C + i1;
+  float u_next = qrow ? __ldg(urow) : 1.0f;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    for (int ii = 0; ii < 32; ii++) {
+      const int i = 32 * k + ii;
+      if (i >= nb) break;
+      if (lane == ii) {
+#pragma unroll
+        for (int rr = 0; rr < RW; rr += 4)
+          *reinterpret_cast<float4 *>(xw + rr) = make_float4(w[rr][k], w[rr + 1][k], w[rr + 2][k], w[rr + 3][k]);
+      }
+      __syncwarp();
+      if (qlane) {
+        const float ui = u_next;
+        if (qrow && i + 1 < nb) u_next = __ldg(urow + i + 1);
+        float ei = 0.0f;
+        if (qrow) {
+          const float wi = xw[lane];
+          const float hii = fmaxf(Hs[i * nb + i], 1e-30f);
+          float m = rintf(__fmul_rn(__fdiv_rn(fabsf(wi), ui), 4.0f));
+          m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
+          const float qi = __fmul_rn(__fmul_rn(wi >= 0.0f ? 1.0f : -1.0f, m), ui);
+          ei = __fdiv_rn(__fsub_rn(wi, qi), hii);
+          Q[rq * C + i1 + i] = qi;
+          E[rq * GQ_BLK + i] = ei;
+        }
+        xe[lane] = ei;
+      }
+      __syncwarp();
+      float ev[RW];
+#pragma unroll
+      for (int rr = 0; rr < RW; rr += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(xe + rr);
+        ev[rr] = v.x; ev[rr + 1] = v.y; ev[rr + 2] = v.z; ev[rr + 3] = v.w;
+      }
+      const float *hrow = Hs + i * nb;
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const int c = lane + 32 * kk;
+        if (kk >= k && c > i && c < nb) {
+          const float h = hrow[c];
+#pragma unroll
+          for (int rr = 0; rr < RW; rr++) w[rr][kk] = fmaf(-ev[rr], h, w[rr][kk]);
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(GQ_THREADS) gptq_block_kernel(float *W, const float *unit, const float *U,
                                                                   float *Q, float *E, int64_t R, int64_t C,
                                                                   int64_t i1, int nb, int64_t bstride_rows,
@@ -1063,20 +1153,35 @@ extern "C" int hif4x_gptq(const float *X, const float *unit, const float *U, int
   if (cudaMemcpyAsync(W, X, sizeof(float) * batch * R * C, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return HIF4X_ERR_LAUNCH;
   const size_t smem = sizeof(float) * GQ_BLK * GQ_BLK;
-  // 4 rows per warp when that still gives two waves of CTAs, else 1
-  const bool four = (int64_t)nblk(R, GQW_WARPS * 4) * batch >= 2 * 148;
+  const size_t smem_x = smem + sizeof(float) * GQW_WARPS * 2 * GQX_MAXRW;
+  // rows per warp: the most (16, 8, 4 with the row-exchange kernel) that still
+  // leaves about eight warps per SM; 1 (owner-lane kernel) for small inputs
+  const int64_t rows_all = R * batch;
+  const int rw = rows_all >= (int64_t)16 * 8 * 148 ? 16 : rows_all >= (int64_t)8 * 8 * 148 ? 8
+               : rows_all >= (int64_t)4 * 8 * 148 ? 4 : 1;
   if (cudaFuncSetAttribute(gptq_block_warp_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
           cudaSuccess ||
-      cudaFuncSetAttribute(gptq_block_warp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaFuncSetAttribute(gptq_block_xch_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_x) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(gptq_block_xch_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_x) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(gptq_block_xch_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_x) !=
           cudaSuccess)
     return HIF4X_ERR_LAUNCH;
   for (int64_t i1 = 0; i1 < C; i1 += GQ_BLK) {
     const int nb = (int)std::min<int64_t>(GQ_BLK, C - i1);
-    if (four)
-      gptq_block_warp_kernel<4><<<dim3(nblk(R, GQW_WARPS * 4), (unsigned)batch), GQW_WARPS * 32, smem, s>>>(
+    const dim3 block(GQW_WARPS * 32);
+    if (rw == 16)
+      gptq_block_xch_kernel<16><<<dim3(nblk(R, GQW_WARPS * 16), (unsigned)batch), block, smem_x, s>>>(
+          W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
+    else if (rw == 8)
+      gptq_block_xch_kernel<8><<<dim3(nblk(R, GQW_WARPS * 8), (unsigned)batch), block, smem_x, s>>>(
+          W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
+    else if (rw == 4)
+      gptq_block_xch_kernel<4><<<dim3(nblk(R, GQW_WARPS * 4), (unsigned)batch), block, smem_x, s>>>(
           W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
     else
-      gptq_block_warp_kernel<1><<<dim3(nblk(R, GQW_WARPS), (unsigned)batch), GQW_WARPS * 32, smem, s>>>(
+      gptq_block_warp_kernel<1><<<dim3(nblk(R, GQW_WARPS), (unsigned)batch), block, smem, s>>>(
           W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
     HIF4X_CHECK_LAUNCH();
     const int64_t i2 = i1 + nb;

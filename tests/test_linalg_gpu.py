@@ -177,3 +177,20 @@ def test_make_R_matches_reference_construction():
     d = (torch.rand(dh, generator=g) < 0.5).float() * 2 - 1
     assert torch.equal(att.make_R(dh, "cuda").cpu(), H * d.unsqueeze(0))
     assert att.make_R(96, "cuda") is None
+
+
+@pytest.mark.parametrize("R,batch", [(19000, 1), (9600, 1), (4800, 1), (2400, 8)])
+def test_gptq_row_exchange_identical(R, batch):
+    """The row-exchange kernels (16, 8 or 4 rows per warp, picked by the row
+    count) give the same bits as the one-row-per-warp kernel that small inputs
+    take: GPTQ rows are independent, so a 64-row slice is a small input."""
+    C = 260   # a partial second 128-column block
+    x = rnd(batch, R, C, seed=R + batch, scale=0.02)
+    U = torch.stack([la.chol_upper_inv(a.T @ a) for a in rnd(batch, 3 * C, C, seed=5 + R)])
+    unit = codec.unit_flat(codec.encode(x.reshape(batch * R, C)[:, :256].contiguous()))
+    unit = torch.cat([unit, unit[:, :C - 256]], 1).reshape(batch, R, C).contiguous()
+    got = la.gptq(x, unit, U)
+    for b in range(batch):
+        for r0 in (0, R - 64):
+            small = la.gptq(x[b, r0:r0 + 64].contiguous(), unit[b, r0:r0 + 64].contiguous(), U[b])
+            assert torch.equal(got[b, r0:r0 + 64], small), (b, r0)
