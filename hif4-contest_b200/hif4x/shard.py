@@ -81,6 +81,15 @@ def pack_params(p: dict) -> torch.Tensor:
     return torch.cat([meta.view(torch.uint8).reshape(-1), codes.reshape(-1)])
 
 
+def unpack_params(buf: torch.Tensor, R: int, C: int):
+    """(meta (R, C/64) int32, codes (R, C/2) uint8) views of a pack_params buffer."""
+    nm = R * (C // 64) * 4
+    codes = buf[nm:nm + R * C // 2].view(R, C // 2)
+    if codes.data_ptr() % 16:     # the decode kernels load codes in 16-byte vectors
+        codes = codes.clone()
+    return buf[:nm].view(torch.int32).view(R, C // 64), codes
+
+
 def gather_shards(local: dict[str, torch.Tensor], dist, device) -> dict[str, torch.Tensor] | None:
     """All ranks: contribute {key: uint8 CUDA buffer}; rank 0 receives every
     rank's buffers (one all_gather of sizes, one of padded payloads, NCCL)."""

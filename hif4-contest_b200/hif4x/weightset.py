@@ -28,12 +28,17 @@ def _worker_stream(dev, i: int) -> torch.cuda.Stream:
     return _STREAMS[key]
 
 
-def convert(jobs: list, workers: int = 2, device=None) -> dict:
+def convert(jobs: list, workers: int = 2, device=None, consume=None) -> dict:
     """jobs: [(key, weight_pair, calib_pairs, test_pair or None)], pairs as
     the six-function API takes them (CPU or CUDA tensors).  Returns
     {key: (calibration result, dynamic result or None)} with every tensor left
-    on the GPU.  Work is taken from the list in order by `workers` threads, so
-    list the longest matrices first (shard.matrix_cost)."""
+    on the GPU, or {key: consume(key, result, dynamic)} when `consume` is
+    given: it runs on the worker's thread and stream as each matrix finishes,
+    so a caller that packs or offloads there holds one matrix's full-precision
+    outputs at a time instead of the whole set's (a 32-layer weight set's
+    dict5 and states exceed one GPU's memory).  Work is taken from the list in
+    order by `workers` threads, so list the longest matrices first
+    (shard.matrix_cost)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     out: dict = {}
     errors: list = []
@@ -57,8 +62,10 @@ def convert(jobs: list, workers: int = 2, device=None) -> dict:
                     if test is not None:
                         dyn = linear.dynamic_activation(test[0], test[1], res["activation_state"],
                                                         return_device=True)
+                    val = consume(key, res, dyn) if consume is not None else (res, dyn)
+                    del res, dyn
                     with lock:
-                        out[key] = (res, dyn)
+                        out[key] = val
                 except Exception as e:  # re-raised in the caller
                     with lock:
                         errors.append(e)
