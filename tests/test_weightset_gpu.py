@@ -39,3 +39,35 @@ def test_concurrent_matches_sequential():
         dref = linear.dynamic_activation(test[0], test[1], ref["activation_state"], return_device=True)
         for k in ("sf", "lv2", "lv3", "sign", "mant"):
             assert torch.equal(getattr(dyn, k), getattr(dref, k)), (key, k)
+
+
+def test_consume_callback_packs_each_matrix():
+    """consume() runs once per matrix on its worker and its return value is
+    what convert() keeps: packed weights equal packing the full results."""
+    from hif4x import codec, shard
+    names = ["lin_c1024", "lin_c2560"]
+    jobs = []
+    for name in names:
+        wpair, calib, tests, _ = pc.linear_inputs(name)
+        jobs.append((name, _dev(wpair), [_dev(c) for c in calib], _dev(tests[0])))
+    seen = []
+
+    def consume(key, res, dyn):
+        seen.append(key)
+        return shard.pack_params(res["weight_params"]), codec.pack(dyn)
+
+    got = weightset.convert(jobs, workers=2, consume=consume)
+    assert sorted(seen) == sorted(names) and sorted(got) == sorted(names)
+    full = weightset.convert(jobs, workers=1)
+    for key, wpair, _, _ in jobs:
+        res, dyn = full[key]
+        buf, (meta, codes) = got[key]
+        assert torch.equal(buf, shard.pack_params(res["weight_params"]))
+        m2, c2 = codec.pack(dyn)
+        assert torch.equal(meta, m2) and torch.equal(codes, c2)
+        N, C = wpair[0].shape
+        wm, wc = shard.unpack_params(buf, N, C)
+        w_hat = codec.decode_packed(wm, wc, torch.float32)
+        assert torch.equal(w_hat, codec.decode(codec.Dict5(*(
+            res["weight_params"][k].reshape(N, -1).contiguous() for k in
+            ("scale_factor", "scale_lv2", "scale_lv3", "sign", "mant")))))
