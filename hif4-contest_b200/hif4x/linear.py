@@ -488,6 +488,8 @@ def dynamic_activation(activation_quant: torch.Tensor, activation_scale: torch.T
     dev = _dev()
     q, sc = upload_pair((activation_quant, activation_scale), dev)
     R, C = q.shape
+    if R == 0:   # the reference's per-group amax() raises on an empty input
+        raise RuntimeError("hif4_dynamic_quantize_activation: empty activation (0 rows)")
     st = activation_state if isinstance(activation_state, dict) else {}
     s = None
     t = st.get("s")

@@ -116,7 +116,28 @@ def main():
                 out[f"{name}/t{i}/{role}_meta"], out[f"{name}/t{i}/{role}_codes"] = m, c
         print(name, "rot", qs["rot"], "gq", qs.get("gq", 0),
               "score", [round(1 - out[f"{name}/t{i}/mse"] / out[f"{name}/t{i}/mse_std"], 4) for i in range(len(tests))])
-    for name in pc.ATTN_VC_CASES:
+    for name in pc.EDGE_LINEAR_CASES:
+        if args.only and name not in args.only:
+            continue
+        wpair, calib, tests, digest = pc.edge_linear_inputs(name)
+        res = sol.hif4_calibration_and_quantize_weight(wpair[0], wpair[1], calib)
+        st = res["activation_state"]
+        out[f"{name}/digest"] = np.frombuffer(bytes.fromhex(digest), np.uint8)
+        for k in ("mode", "g", "tmax"):
+            out[f"{name}/{k}"] = np.int64(st[k])
+        out[f"{name}/has_gw"] = np.int64(st["gw"] is not None)
+        out[f"{name}/w_meta"], out[f"{name}/w_codes"] = packed(res["weight_params"])
+        W = pc.deq_nvfp4(wpair)
+        Wq = pc.deq_dict5(res["weight_params"])
+        for i, tp in enumerate(tests):
+            sol._QKV_CARRY.clear()
+            pa = sol.hif4_dynamic_quantize_activation(tp[0], tp[1], st)
+            X = pc.deq_nvfp4(tp)
+            out[f"{name}/t{i}/mse"] = np.float64(((pc.deq_dict5(pa) @ Wq.T - X @ W.T) ** 2).mean())
+            out[f"{name}/t{i}/meta"], out[f"{name}/t{i}/codes"] = packed(pa)
+        print(name, "mode", st["mode"], "g", st["g"], "tmax", st["tmax"])
+
+    for name in list(pc.ATTN_VC_CASES) + list(pc.ATTN_EDGE_CASES):
         if args.only and name not in args.only:
             continue
         (qh, kvh, dh), calib, tests, digest = pc.attn_inputs(name)

@@ -49,6 +49,38 @@ ATTN_VC_CASES = {
 }
 
 
+# edge cases of the linear path: name -> (N, C, calib rows, test rows, seed, zero)
+# (zero = all-zero weight and activations: every Hessian is 0 and every group
+# takes the smallest E6M2 scale; test rows down to a single token)
+EDGE_LINEAR_CASES = {
+    "edge_zero": (128, 256, (64, 64, 64), (1, 3), 11, True),
+    "edge_tiny": (128, 256, (64, 64, 64), (1, 2), 12, False),
+}
+
+# attention edge case: single-token and 3-token inputs, q -> k -> v in one
+# process (the compensation runs at T = 1)
+ATTN_EDGE_CASES = {
+    "attn_edge_t1": (4, 2, 64, (8, 8, 8), (1, 3), 13),
+}
+
+
+def edge_linear_inputs(name: str):
+    N, C, calib_rows, test_rows, seed, zero = EDGE_LINEAR_CASES[name]
+    h = hashlib.sha256()
+    g = torch.Generator().manual_seed(seed)
+
+    def mk(R, scale):
+        x = torch.zeros(R, C) if zero else torch.randn(R, C, generator=g) * scale
+        p = synth.quantize_nvfp4(x.to(torch.bfloat16))
+        _digest(h, p)
+        return list(synth.reference_form(*p))
+
+    w = mk(N, 0.02)
+    calib = [mk(T, 1.0) for T in calib_rows]
+    tests = [mk(T, 1.0) for T in test_rows]
+    return w, calib, tests, h.hexdigest()
+
+
 def _digest(h, packed):
     for t in packed[:2]:
         h.update(t.numpy().tobytes())
@@ -75,7 +107,7 @@ def linear_inputs(name: str):
 
 
 def attn_inputs(name: str):
-    qh, kvh, dh, calib_T, test_T, seed = ATTN_CASES[name] if name in ATTN_CASES else ATTN_VC_CASES[name]
+    qh, kvh, dh, calib_T, test_T, seed = {**ATTN_CASES, **ATTN_VC_CASES, **ATTN_EDGE_CASES}[name]
     h = hashlib.sha256()
 
     def sample(s, T):

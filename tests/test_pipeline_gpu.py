@@ -47,6 +47,10 @@ def mismatch(p: dict, meta_ref, codes_ref) -> float:
 
 
 def check_mse(name, got, want, std, report):
+    if want == 0.0:
+        report.append(f"{name}: mse {got:.4e} ref 0")
+        assert got == 0.0, report[-1]
+        return
     rel = got / want - 1.0
     report.append(f"{name}: mse {got:.4e} ref {want:.4e} ({100 * rel:+.2f} %), score {1 - got / std:.4f} "
                   f"ref {1 - want / std:.4f}")
@@ -113,7 +117,7 @@ def test_attention_case(name, gold, capsys):
         print("\n  " + "\n  ".join(report))
 
 
-@pytest.mark.parametrize("name", list(pc.ATTN_VC_CASES))
+@pytest.mark.parametrize("name", list(pc.ATTN_VC_CASES) + list(pc.ATTN_EDGE_CASES))
 def test_attention_vcomp_case(name, gold, capsys):
     """q -> k -> v in one process: the v call compensates against the carried
     q and k (solution.py:1288-1394) exactly when the reference's did, and the
@@ -143,3 +147,47 @@ def test_attention_vcomp_case(name, gold, capsys):
                   float(gold[f"{name}/t{i}/mse_std"]), report)
     with capsys.disabled():
         print("\n  " + "\n  ".join(report))
+
+
+@pytest.mark.parametrize("name", list(pc.EDGE_LINEAR_CASES))
+def test_linear_edge_case(name, gold, capsys):
+    """All-zero weight and activations (zero Hessians, smallest E6M2 scale) and
+    single-token dynamic calls: the reference's decisions, its codes exactly
+    for the all-zero case, and its output MSE within 1 % otherwise."""
+    wpair, calib, tests, digest = pc.edge_linear_inputs(name)
+    assert bytes(gold[f"{name}/digest"]).hex() == digest
+    res = solution.hif4_calibration_and_quantize_weight(wpair[0], wpair[1], calib)
+    st = res["activation_state"]
+    assert not hif4_errors(res["weight_params"], wpair[0].shape) and not state_errors(st)
+    for k in ("mode", "g", "tmax"):
+        assert st[k] == int(gold[f"{name}/{k}"]), k
+    assert (st["gw"] is not None) == bool(gold[f"{name}/has_gw"])
+    zero = pc.EDGE_LINEAR_CASES[name][5]
+    wm = mismatch(res["weight_params"], gold[f"{name}/w_meta"], gold[f"{name}/w_codes"])
+    report = [f"weight code mismatch {100 * wm:.2f} %"]
+    if zero:
+        assert wm == 0.0
+    W = pc.deq_nvfp4(wpair)
+    Wq = pc.deq_dict5(res["weight_params"])
+    for i, tp in enumerate(tests):
+        pa = solution.hif4_dynamic_quantize_activation(tp[0], tp[1], st)
+        assert not hif4_errors(pa, tp[0].shape)
+        m = mismatch(pa, gold[f"{name}/t{i}/meta"], gold[f"{name}/t{i}/codes"])
+        report.append(f"t{i} (T={tp[0].shape[0]}) code mismatch {100 * m:.2f} %")
+        if zero:
+            assert m == 0.0
+        X = pc.deq_nvfp4(tp)
+        mse = float(((pc.deq_dict5(pa) @ Wq.T - X @ W.T) ** 2).mean())
+        check_mse(f"{name}/t{i}", mse, float(gold[f"{name}/t{i}/mse"]), float("nan"), report)
+    with capsys.disabled():
+        print("\n  " + "\n  ".join(report))
+
+
+def test_empty_activation_raises():
+    """A 0-token activation raises, as the reference's amax() over an empty
+    tensor does."""
+    wpair, calib, tests, _ = pc.edge_linear_inputs("edge_tiny")
+    st = solution.hif4_calibration_and_quantize_weight(wpair[0], wpair[1], calib)["activation_state"]
+    q, s = tests[0]
+    with pytest.raises(RuntimeError):
+        solution.hif4_dynamic_quantize_activation(q[:0], s[:0], st)
