@@ -620,26 +620,47 @@ __global__ void zero_upper_kernel(float *A, int64_t n, int64_t total) {
 }
 
 // --------------------------------------------------------------------------
-// GPTQ: one CTA of 128 threads per 128 rows; thread t owns row r0 + t.
-// For the column block [i1, i1+nb): quantize column i to the unit grid
+// GPTQ, one 128-column block at a time (kernels below, trailing update as a
+// GEMM in hif4x_gptq).  For the column block [i1, i1+nb): quantize column i
+// to the unit grid
 //   m = clamp(round(|w| / u * 4), 0, 7) * 0.25;  q = (w >= 0 ? 1 : -1) * m * u
 // record E[:, i] = (w - q) / U[i][i] and propagate w[:, j] -= E[:, i] * U[i][j]
 // for j > i inside the block (example/solution/solution.py:316-326).
-constexpr int GQ_THREADS = 128;
 constexpr int GQ_BLK = 128;
-constexpr int GQW_WARPS = 8;   // warps per CTA in the warp-per-rows kernel
+constexpr int GQW_WARPS = 8;   // warps per CTA of the GPTQ block kernels
 
-// Warp-per-rows form: each warp owns GQW_ROWS rows; lane l holds block
-// columns l, l+32, l+64, l+96 of each of them in registers.  Column i's owner
-// lane quantizes it for all of the warp's rows (independent chains, so their
-// latencies overlap), broadcasts the scaled errors, and every lane updates its
-// own later columns; one shared-memory read of U's row serves all the rows.
-// U's block sits in shared memory.
-template <int GQW_ROWS>
-__global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_warp_kernel(float *W, const float *unit, const float *U,
-                                                                         float *Q, float *E, int64_t R, int64_t C,
-                                                                         int64_t i1, int nb, int64_t bstride_rows,
-                                                                         int64_t bstride_u) {
+// U's nb x nb diagonal block at (i1, i1) into shared memory (row-major, nb
+// per row).  A full 128-column block on 16-byte-aligned rows goes as 16
+// independent float4 loads per thread (no index division): the small-input
+// GPTQ launches run a few CTAs and were waiting on exactly this load.
+__device__ __forceinline__ void gptq_load_u_block(float *Hs, const float *U, int64_t C, int64_t i1, int nb) {
+  const float *base = U + i1 * C + i1;
+  if (nb == GQ_BLK && (C & 3) == 0 && (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && blockDim.x == 256) {
+    float4 v[16];
+#pragma unroll
+    for (int q = 0; q < 16; q++) {
+      const int e = threadIdx.x + 256 * q;   // float4 index: row e / 32, column 4 (e % 32)
+      v[q] = __ldg(reinterpret_cast<const float4 *>(base + (int64_t)(e >> 5) * C) + (e & 31));
+    }
+#pragma unroll
+    for (int q = 0; q < 16; q++) reinterpret_cast<float4 *>(Hs)[threadIdx.x + 256 * q] = v[q];
+    return;
+  }
+  for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
+}
+
+// One-row-per-warp form for small inputs (proxies, hold-outs, short dynamic
+// calls, a few thousand weight rows), where latency, not issue, sets the time.
+// Lane l holds block columns l, l+32, l+64, l+96 of the warp's row.  For
+// column i the owner's value is broadcast first and every lane rounds it (the
+// warp issues the rounding once either way, without a divergent branch or a
+// second shuffle); the unit, U[i][i] and U's row are loaded a column ahead.
+// The operations and their order are those of the row-exchange kernel below,
+// so the results are identical.
+__global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_row_kernel(float *W, const float *unit, const float *U,
+                                                                        float *Q, float *E, int64_t R, int64_t C,
+                                                                        int64_t i1, int nb, int64_t bstride_rows,
+                                                                        int64_t bstride_u) {
   extern __shared__ float Hs[];   // [nb][nb]
   const int64_t bz = blockIdx.y;
   W += bz * bstride_rows * C;
@@ -647,70 +668,58 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_warp_kernel(float *
   Q += bz * bstride_rows * C;
   E += bz * bstride_rows * GQ_BLK;
   U += bz * bstride_u;
-  for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
+  gptq_load_u_block(Hs, U, C, i1, nb);
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t r0 = ((int64_t)blockIdx.x * GQW_WARPS + (threadIdx.x >> 5)) * GQW_ROWS;
-  if (r0 >= R) return;
-  float w[GQW_ROWS][4], u[GQW_ROWS][4], q[GQW_ROWS][4], err[GQW_ROWS][4];
+  const int64_t r = (int64_t)blockIdx.x * GQW_WARPS + (threadIdx.x >> 5);
+  if (r >= R) return;
+  float w[4], qk[4], ek[4];
 #pragma unroll
-  for (int rr = 0; rr < GQW_ROWS; rr++) {
-    const int64_t r = r0 + rr;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int c = lane + 32 * k;
-      const bool in = r < R && c < nb;
-      w[rr][k] = in ? W[r * C + i1 + c] : 0.0f;
-      u[rr][k] = in ? unit[r * C + i1 + c] : 1.0f;
-      q[rr][k] = 0.0f;
-      err[rr][k] = 0.0f;
-    }
+  for (int k = 0; k < 4; k++) {
+    const int c = lane + 32 * k;
+    w[k] = c < nb ? W[r * C + i1 + c] : 0.0f;
+    qk[k] = 0.0f;
+    ek[k] = 0.0f;
   }
+  const float *urow = unit + r * C + i1;
+  float u_next = __ldg(urow);
+  float h_next = Hs[0];
 #pragma unroll
   for (int k = 0; k < 4; k++) {
     for (int ii = 0; ii < 32; ii++) {
       const int i = 32 * k + ii;
       if (i >= nb) break;
-      float ei[GQW_ROWS];
-      const float hii = fmaxf(Hs[i * nb + i], 1e-30f);
-#pragma unroll
-      for (int rr = 0; rr < GQW_ROWS; rr++) {
-        ei[rr] = 0.0f;
-        if (lane == ii) {
-          const float wi = w[rr][k], ui = u[rr][k];
-          float m = rintf(__fmul_rn(__fdiv_rn(fabsf(wi), ui), 4.0f));
-          m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
-          const float qi = __fmul_rn(__fmul_rn(wi >= 0.0f ? 1.0f : -1.0f, m), ui);
-          q[rr][k] = qi;
-          ei[rr] = __fdiv_rn(__fsub_rn(wi, qi), hii);
-          err[rr][k] = ei[rr];
-        }
+      const float ui = u_next, hii = fmaxf(h_next, 1e-30f);
+      if (i + 1 < nb) {
+        u_next = __ldg(urow + i + 1);
+        h_next = Hs[(i + 1) * nb + i + 1];
       }
-#pragma unroll
-      for (int rr = 0; rr < GQW_ROWS; rr++) ei[rr] = __shfl_sync(0xffffffffu, ei[rr], ii);
       const float *hrow = Hs + i * nb;
+      float hv[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) hv[kk] = (kk >= k && lane + 32 * kk < nb) ? hrow[lane + 32 * kk] : 0.0f;
+      const float wi = __shfl_sync(0xffffffffu, w[k], ii);
+      float m = rintf(__fmul_rn(__fdiv_rn(fabsf(wi), ui), 4.0f));
+      m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
+      const float qi = __fmul_rn(__fmul_rn(wi >= 0.0f ? 1.0f : -1.0f, m), ui);
+      const float ei = __fdiv_rn(__fsub_rn(wi, qi), hii);
+      if (lane == ii) {
+        qk[k] = qi;
+        ek[k] = ei;
+      }
 #pragma unroll
       for (int kk = 0; kk < 4; kk++) {
         const int c = lane + 32 * kk;
-        if (kk >= k && c > i && c < nb) {
-          const float h = hrow[c];
-#pragma unroll
-          for (int rr = 0; rr < GQW_ROWS; rr++) w[rr][kk] = fmaf(-ei[rr], h, w[rr][kk]);
-        }
+        if (kk >= k && c > i && c < nb) w[kk] = fmaf(-ei, hv[kk], w[kk]);
       }
     }
   }
 #pragma unroll
-  for (int rr = 0; rr < GQW_ROWS; rr++) {
-    const int64_t r = r0 + rr;
-    if (r >= R) break;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int c = lane + 32 * k;
-      if (c < nb) {
-        Q[r * C + i1 + c] = q[rr][k];
-        E[r * GQ_BLK + c] = err[rr][k];
-      }
+  for (int k = 0; k < 4; k++) {
+    const int c = lane + 32 * k;
+    if (c < nb) {
+      Q[r * C + i1 + c] = qk[k];
+      E[r * GQ_BLK + c] = ek[k];
     }
   }
 }
@@ -721,7 +730,7 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_warp_kernel(float *
 // 0..RW-1 quantize one row each (the warp issues the quantisation once, not
 // once per row), publish the scaled errors back, and every lane updates its
 // later columns.  Same operations in the same order as
-// gptq_block_warp_kernel, so the results are identical.
+// gptq_block_row_kernel, so the results are identical.
 constexpr int GQX_MAXRW = 16;
 template <int RW>
 __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_xch_kernel(float *W, const float *unit, const float *U,
@@ -735,7 +744,7 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_xch_kernel(float *W
   Q += bz * bstride_rows * C;
   E += bz * bstride_rows * GQ_BLK;
   U += bz * bstride_u;
-  for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
+  gptq_load_u_block(Hs, U, C, i1, nb);
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float *xw = Hs + GQ_BLK * GQ_BLK + warp * (2 * GQX_MAXRW);
@@ -803,42 +812,6 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_xch_kernel(float *W
       }
     }
   }
-}
-
-__global__ void __launch_bounds__(GQ_THREADS) gptq_block_kernel(float *W, const float *unit, const float *U,
-                                                                  float *Q, float *E, int64_t R, int64_t C,
-                                                                  int64_t i1, int nb, int64_t bstride_rows,
-                                                                  int64_t bstride_u) {
-  extern __shared__ float sm[];
-  float *Hs = sm;                        // [nb][nb] block of U
-  float *Ws = sm + GQ_BLK * GQ_BLK;      // [nb][GQ_THREADS] row slices, column-major per thread
-  const int64_t bz = blockIdx.y;
-  W += bz * bstride_rows * C;
-  unit += bz * bstride_rows * C;
-  Q += bz * bstride_rows * C;
-  E += bz * bstride_rows * GQ_BLK;
-  U += bz * bstride_u;
-  const int t = threadIdx.x;
-  for (int e = t; e < nb * nb; e += GQ_THREADS) Hs[e] = U[(i1 + e / nb) * C + i1 + e % nb];
-  const int64_t r = (int64_t)blockIdx.x * GQ_THREADS + t;
-  const bool live = r < R;
-  if (live)
-    for (int j = 0; j < nb; j++) Ws[j * GQ_THREADS + t] = W[r * C + i1 + j];
-  __syncthreads();
-  if (!live) return;
-  for (int i = 0; i < nb; i++) {
-    const float w = Ws[i * GQ_THREADS + t];
-    const float u = unit[r * C + i1 + i];
-    float m = rintf(__fmul_rn(__fdiv_rn(fabsf(w), u), 4.0f));
-    m = __fmul_rn(fminf(fmaxf(m, 0.0f), 7.0f), 0.25f);
-    const float q = __fmul_rn(__fmul_rn(w >= 0.0f ? 1.0f : -1.0f, m), u);
-    Q[r * C + i1 + i] = q;
-    const float dii = fmaxf(Hs[i * nb + i], 1e-30f);
-    const float err = __fdiv_rn(__fsub_rn(w, q), dii);
-    E[r * GQ_BLK + i] = err;
-    for (int j = i + 1; j < nb; j++) Ws[j * GQ_THREADS + t] = fmaf(-err, Hs[i * nb + j], Ws[j * GQ_THREADS + t]);
-  }
-  for (int j = 0; j < nb; j++) W[r * C + i1 + j] = Ws[j * GQ_THREADS + t];
 }
 
 // --------------------------------------------------------------------------
@@ -1155,11 +1128,11 @@ extern "C" int hif4x_gptq(const float *X, const float *unit, const float *U, int
   const size_t smem = sizeof(float) * GQ_BLK * GQ_BLK;
   const size_t smem_x = smem + sizeof(float) * GQW_WARPS * 2 * GQX_MAXRW;
   // rows per warp: the most (16, 8, 4 with the row-exchange kernel) that still
-  // leaves about eight warps per SM; 1 (owner-lane kernel) for small inputs
+  // leaves about eight warps per SM; 1 (gptq_block_row_kernel) for small inputs
   const int64_t rows_all = R * batch;
   const int rw = rows_all >= (int64_t)16 * 8 * 148 ? 16 : rows_all >= (int64_t)8 * 8 * 148 ? 8
                : rows_all >= (int64_t)4 * 8 * 148 ? 4 : 1;
-  if (cudaFuncSetAttribute(gptq_block_warp_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (cudaFuncSetAttribute(gptq_block_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
           cudaSuccess ||
       cudaFuncSetAttribute(gptq_block_xch_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_x) !=
           cudaSuccess ||
@@ -1181,7 +1154,7 @@ extern "C" int hif4x_gptq(const float *X, const float *unit, const float *U, int
       gptq_block_xch_kernel<4><<<dim3(nblk(R, GQW_WARPS * 4), (unsigned)batch), block, smem_x, s>>>(
           W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
     else
-      gptq_block_warp_kernel<1><<<dim3(nblk(R, GQW_WARPS), (unsigned)batch), block, smem, s>>>(
+      gptq_block_row_kernel<<<dim3(nblk(R, GQW_WARPS), (unsigned)batch), block, smem, s>>>(
           W, unit, U, Q, E, R, C, i1, nb, R, u_batch_stride);
     HIF4X_CHECK_LAUNCH();
     const int64_t i2 = i1 + nb;
