@@ -5,8 +5,6 @@ hand-written kernels from libhif4x.so on the current stream.
 """
 from __future__ import annotations
 
-import ctypes
-
 import torch
 
 from . import _lib as L

@@ -13,7 +13,6 @@ import sys
 
 import numpy as np
 import pytest
-import torch
 
 from conftest import GOLDEN, PKG_DIR
 from contract import hif4_errors, state_errors

@@ -8,7 +8,6 @@ gloo here), so these tests exercise exactly that exchange and the schedule.
 import os
 import socket
 
-import pytest
 import torch
 import torch.multiprocessing as mp
 
