@@ -120,6 +120,13 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(inside), "window": window}
 
 
+def physical_gpu(local_rank: int) -> int:
+    """nvidia-smi's index of this rank's GPU."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    ids = vis.split(",") if vis else []
+    return int(ids[local_rank]) if local_rank < len(ids) and ids[local_rank].strip().isdigit() else local_rank
+
+
 def measured_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -245,9 +252,7 @@ def run_gpu(args, rank, ws, local_rank):
             ev_b.record(stream)
         L.call("hif4x_decode_packed", L.ptr(meta), L.ptr(hcodes), ROWS, COLS, L.ptr(rt), L.DT_BF16, sp)
 
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    phys = int(vis.split(",")[local_rank]) if vis and vis.split(",")[local_rank].strip().isdigit() else local_rank
-    clk = ClockSampler(phys)
+    clk = ClockSampler(physical_gpu(local_rank))
     clk.start()
     time.sleep(0.3)
     for _ in range(args.warmup):
@@ -398,7 +403,10 @@ def run_layer(args, rank, ws, local_rank):
             todo = [(j.key, dev_weights[j.key], dev_inputs[(j.layer, j.input_id)][0],
                      dev_inputs[(j.layer, j.input_id)][1]) for j in order]
             # each matrix packed as it finishes; its dict5 and states are dropped
-            done = weightset.convert(todo, workers=args.workers, device=dev,
+            # the matrices within half of the longest one's cost run on high-priority streams
+            top = shard.matrix_cost(order[0].N, order[0].C, T_cal) if order else 0.0
+            urgent = {j.key for j in order if shard.matrix_cost(j.N, j.C, T_cal) >= 0.5 * top}
+            done = weightset.convert(todo, workers=args.workers, device=dev, urgent=urgent,
                                      consume=lambda key, res, dyn: (shard.pack_params(res["weight_params"]),
                                                                     codec.pack(dyn)))
             for key, (buf, dyn) in done.items():
@@ -416,20 +424,28 @@ def run_layer(args, rank, ws, local_rank):
         if dist is not None:
             dist.barrier(device_ids=[local_rank])
 
+    clk = ClockSampler(physical_gpu(local_rank))
+    clk.start()
+    window = {}
+
     def timed(device_resident: bool) -> float:
         for _ in range(args.warmup):
             step(device_resident)
         torch.cuda.synchronize(dev)
         barrier()
         # CUDA events on the stream every kernel of the step is launched on
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
+        # (the step's worker streams join it before the step returns)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        w0 = time.time()
+        evs[0].record()
+        for k in range(args.steps):
             step(device_resident)
-        e1.record()
+            evs[k + 1].record()
         torch.cuda.synchronize(dev)
-        dt = e0.elapsed_time(e1) / 1e3 / max(args.steps, 1)
+        if device_resident:
+            window["w"] = (w0, time.time())
+            window["step_ms"] = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
+        dt = evs[0].elapsed_time(evs[-1]) / 1e3 / max(args.steps, 1)
         if dist is not None:
             t = torch.tensor([dt], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -438,6 +454,7 @@ def run_layer(args, rank, ws, local_rank):
 
     compact_api = False
     dt = timed(True)
+    clk.stop()
     dev_packed = dict(packed)   # the device-resident run's weights, for the quality below
     dt_api = dt_api_compact = None
     if not args.no_e2e:
@@ -483,6 +500,7 @@ def run_layer(args, rank, ws, local_rank):
                                "dynamic tokens per matrix",
                    "parallelism": f"LPT over {ws} GPU(s), {args.workers} concurrent matrices per GPU"},
         "weight_gelem_per_s": elems / dt / 1e9, "gather_s": gather_s,
+        "step_ms_rank0": window["step_ms"], "clocks": clk.summary(*window["w"]),
         "quality": {"mean_rel_output_mse": float(q[0] / q[2]), "max_rel_output_mse": float(q[3]),
                     "mean_score_vs_alg1": float(q[1] / q[2]), "matrices": int(q[2]),
                     "note": "|X W^T - X^ W^^T|^2 / |X W^T|^2 on each matrix's 1024-token test input; "
@@ -542,19 +560,24 @@ def run_attention(args, rank, ws, local_rank):
             pv = attention.dynamic_v(test["v"][0], test["v"][1], st["v_state"], kvh, dh, return_device=True)
             outs[b] = (pq, pk, pv)
 
+    clk = ClockSampler(physical_gpu(local_rank))
+    clk.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier(device_ids=[local_rank])
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    w0 = time.time()
+    evs[0].record()
+    for k in range(args.steps):
         step()
-    e1.record()
+        evs[k + 1].record()
     torch.cuda.synchronize(dev)
-    dt = e0.elapsed_time(e1) / 1e3 / max(args.steps, 1)
+    w1 = time.time()
+    clk.stop()
+    step_ms = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
+    dt = evs[0].elapsed_time(evs[-1]) / 1e3 / max(args.steps, 1)
     # quality on this rank's first item: converted vs bf16 attention output
     rel = float("nan")
     sc = {}
@@ -584,6 +607,7 @@ def run_attention(args, rank, ws, local_rank):
                    "parallelism": f"batch items round-robin over {ws} GPU(s)"},
         "quality": {"rel_err_softmax_qkv": rel, "item": mine[0] if mine else None,
                     "rel_output_mse_vs_nvfp4": sc.get("rel_mse"), "score_vs_alg1": sc.get("score")},
+        "step_ms_rank0": step_ms, "clocks": clk.summary(w0, w1),
         "timing_note": "CUDA events on the launching stream, max over ranks",
     }), flush=True)
 

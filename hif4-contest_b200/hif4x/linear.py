@@ -93,10 +93,12 @@ _SIDE: dict = {}
 
 def _side_stream(dev) -> torch.cuda.Stream:
     """A second stream for independent calibration branches, one per
-    (device, main stream), so concurrent calibrations keep theirs apart."""
-    key = (str(dev), torch.cuda.current_stream(dev).cuda_stream)
+    (device, main stream), so concurrent calibrations keep theirs apart; it
+    takes the main stream's priority."""
+    main = torch.cuda.current_stream(dev)
+    key = (str(dev), main.cuda_stream)
     if key not in _SIDE:
-        _SIDE[key] = torch.cuda.Stream(device=dev)
+        _SIDE[key] = torch.cuda.Stream(device=dev, priority=main.priority)
     return _SIDE[key]
 
 

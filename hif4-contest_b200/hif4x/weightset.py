@@ -19,16 +19,17 @@ from . import linear
 _STREAMS: dict = {}
 
 
-def _worker_stream(dev, i: int) -> torch.cuda.Stream:
-    """Worker i's stream on `dev`, created once: the caching allocator keeps
-    memory per stream, so fresh streams on every call would re-allocate."""
-    key = (str(dev), i)
+def _worker_stream(dev, i: int, urgent: bool = False) -> torch.cuda.Stream:
+    """Worker i's stream on `dev` (a high-priority one for urgent matrices),
+    created once: the caching allocator keeps memory per stream, so fresh
+    streams on every call would re-allocate."""
+    key = (str(dev), i, urgent)
     if key not in _STREAMS:
-        _STREAMS[key] = torch.cuda.Stream(device=dev)
+        _STREAMS[key] = torch.cuda.Stream(device=dev, priority=-1 if urgent else 0)
     return _STREAMS[key]
 
 
-def convert(jobs: list, workers: int = 2, device=None, consume=None) -> dict:
+def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None) -> dict:
     """jobs: [(key, weight_pair, calib_pairs, test_pair or None)], pairs as
     the six-function API takes them (CPU or CUDA tensors).  Returns
     {key: (calibration result, dynamic result or None)} with every tensor left
@@ -38,23 +39,28 @@ def convert(jobs: list, workers: int = 2, device=None, consume=None) -> dict:
     outputs at a time instead of the whole set's (a 32-layer weight set's
     dict5 and states exceed one GPU's memory).  Work is taken from the list in
     order by `workers` threads, so list the longest matrices first
-    (shard.matrix_cost)."""
+    (shard.matrix_cost).  Matrices whose key is in `urgent` run on
+    high-priority streams: the block scheduler gives their kernels the next
+    free SMs, so the serial chains of a long matrix (the Cholesky leaves and
+    GPTQ column blocks, one CTA each) do not queue behind the many-CTA
+    kernels of the shorter matrices beside it."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     out: dict = {}
     errors: list = []
     lock = threading.Lock()
     nxt = [0]
 
+    urgent = set(urgent or ())
+
     def work(i: int):
         torch.cuda.set_device(dev)
-        stream = _worker_stream(dev, i)
-        with torch.cuda.stream(stream):
-            while True:
-                with lock:
-                    if errors or nxt[0] >= len(jobs):
-                        break
-                    key, wpair, calib, test = jobs[nxt[0]]
-                    nxt[0] += 1
+        while True:
+            with lock:
+                if errors or nxt[0] >= len(jobs):
+                    break
+                key, wpair, calib, test = jobs[nxt[0]]
+                nxt[0] += 1
+            with torch.cuda.stream(_worker_stream(dev, i, key in urgent)):
                 try:
                     res = linear.calibrate_weight(wpair[0], wpair[1], calib, return_device=True,
                                                   rng=torch.Generator().manual_seed(0))
@@ -70,11 +76,13 @@ def convert(jobs: list, workers: int = 2, device=None, consume=None) -> dict:
                     with lock:
                         errors.append(e)
                     break
-        stream.synchronize()
+        for u in (False, True):
+            _worker_stream(dev, i, u).synchronize()
 
     workers = max(1, min(workers, len(jobs)))
     for i in range(workers):   # order every worker after the caller's pending work (its inputs)
-        _worker_stream(dev, i).wait_stream(torch.cuda.current_stream(dev))
+        for u in (False, True):
+            _worker_stream(dev, i, u).wait_stream(torch.cuda.current_stream(dev))
     if workers == 1:
         work(0)
     else:
