@@ -71,3 +71,23 @@ def test_consume_callback_packs_each_matrix():
         assert torch.equal(w_hat, codec.decode(codec.Dict5(*(
             res["weight_params"][k].reshape(N, -1).contiguous() for k in
             ("scale_factor", "scale_lv2", "scale_lv3", "sign", "mant")))))
+
+
+def test_urgent_streams_same_results():
+    """Matrices marked urgent run on high-priority streams (their side
+    streams too) and give exactly the results of the normal-priority run."""
+    names = ["lin_c1024", "lin_c2560", "lin_c4224"]
+    jobs = []
+    for name in names:
+        wpair, calib, tests, _ = pc.linear_inputs(name)
+        jobs.append((name, _dev(wpair), [_dev(c) for c in calib], _dev(tests[0])))
+    plain = weightset.convert(jobs, workers=2)
+    hi = weightset.convert(jobs, workers=2, urgent={"lin_c4224", "lin_c1024"})
+    for key in names:
+        (r0, d0), (r1, d1) = plain[key], hi[key]
+        for k in r0["weight_params"]:
+            assert torch.equal(r0["weight_params"][k], r1["weight_params"][k]), (key, k)
+        for k in ("sf", "lv2", "lv3", "sign", "mant"):
+            assert torch.equal(getattr(d0, k), getattr(d1, k)), (key, k)
+    assert weightset._worker_stream(torch.device("cuda", 0), 0, True).priority < \
+        weightset._worker_stream(torch.device("cuda", 0), 0, False).priority
