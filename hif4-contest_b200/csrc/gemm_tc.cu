@@ -71,11 +71,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 // bounded wait: false (and the device status set) if the phase never completes
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  for (long long i = 0; i < SPIN_LIMIT; i++)
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, long long limit) {
+  for (long long i = 0; i < limit; i++)
     if (mbar_try_wait(bar, parity)) return true;
   atomicExch(&g_status, HIF4X_TIMEOUT);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  return mbar_wait_limit(bar, parity, SPIN_LIMIT);
+}
+
+// The failure path of the bounded wait, run on its own: one thread waits on an
+// mbarrier that nothing arrives on (no copy or MMA is ever in flight here), so
+// the wait runs out after `limit` polls and records HIF4X_TIMEOUT.
+__global__ void wait_selftest_kernel(long long limit, int *done) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const bool ok = mbar_wait_limit(&bar, 0, limit);
+  *done = ok ? 1 : 2;
 }
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, void *dst, uint64_t *bar, int x, int y) {
@@ -579,8 +593,20 @@ int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alph
   return st;
 }
 
+// Runs wait_selftest_kernel with a spin limit of `spins` polls (1 .. 2^22)
+// and returns once it has finished; *done_dev is set to 2 when the wait ran
+// out (it always does: nothing arrives), and the device status then reads
+// HIF4X_TIMEOUT.
+extern "C" int hif4x_wait_selftest(long long spins, int *done_dev, void *stream) {
+  if (spins < 1 || spins > tc::SPIN_LIMIT || !done_dev) return HIF4X_ERR_ARG;
+  tc::wait_selftest_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(spins, done_dev);
+  HIF4X_CHECK_LAUNCH();
+  return cudaStreamSynchronize((cudaStream_t)stream) == cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
+}
+
 // Synchronises the stream and reports (then clears) the sticky device status
-// set by bounded waits that expired: HIF4X_OK or HIF4X_TIMEOUT.
+// set by bounded waits that expired: HIF4X_OK or HIF4X_TIMEOUT.  The word is
+// one per device, not per stream: a read from any stream clears it for all.
 extern "C" int hif4x_device_status(void *stream) {
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return HIF4X_ERR_LAUNCH;
   int st = 0;

@@ -625,7 +625,9 @@ __global__ void zero_upper_kernel(float *A, int64_t n, int64_t total) {
 // to the unit grid
 //   m = clamp(round(|w| / u * 4), 0, 7) * 0.25;  q = (w >= 0 ? 1 : -1) * m * u
 // record E[:, i] = (w - q) / U[i][i] and propagate w[:, j] -= E[:, i] * U[i][j]
-// for j > i inside the block (example/solution/solution.py:316-326).
+// for j > i inside the block (example/solution/solution.py:316-326).  Every
+// step rounds as the reference's elementwise torch/numpy ops do: the
+// propagation is a rounded product then a rounded subtraction, never an FMA.
 constexpr int GQ_BLK = 128;
 constexpr int GQW_WARPS = 8;   // warps per CTA of the GPTQ block kernels
 
@@ -710,7 +712,7 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_row_kernel(float *W
 #pragma unroll
       for (int kk = 0; kk < 4; kk++) {
         const int c = lane + 32 * kk;
-        if (kk >= k && c > i && c < nb) w[kk] = fmaf(-ei, hv[kk], w[kk]);
+        if (kk >= k && c > i && c < nb) w[kk] = __fsub_rn(w[kk], __fmul_rn(ei, hv[kk]));
       }
     }
   }
@@ -807,7 +809,7 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_xch_kernel(float *W
         if (kk >= k && c > i && c < nb) {
           const float h = hrow[c];
 #pragma unroll
-          for (int rr = 0; rr < RW; rr++) w[rr][kk] = fmaf(-ev[rr], h, w[rr][kk]);
+          for (int rr = 0; rr < RW; rr++) w[rr][kk] = __fsub_rn(w[rr][kk], __fmul_rn(ev[rr], h));
         }
       }
     }
@@ -822,6 +824,9 @@ __global__ void __launch_bounds__(GQW_WARPS * 32) gptq_block_xch_kernel(float *W
 //   v4[idx] += dr (dr = +1 if M[idx] < 0 else -1) and M += dr * d[idx] * G[idx].
 // A row without an improving legal flip never flips again (its state does not
 // change), so it stops.  Each thread owns RC columns in registers.
+// Both g = d2col + |M|*(-2d) and M += coef*G[idx] are a rounded product then
+// a rounded sum, as the reference's addcmul / numpy ops on the CPU (no FMA,
+// solution.py:474-521, 541-546, 595), so near-ties resolve as they do there.
 constexpr int RC = 8;
 
 __global__ void __launch_bounds__(1024) refine_rows_kernel(float *M, float *v4, const float *d, const float *G,
@@ -857,7 +862,7 @@ __global__ void __launch_bounds__(1024) refine_rows_kernel(float *M, float *v4, 
       if (c < C) {
         const bool up = m[k] < 0.0f;
         const bool ill = up ? (v[k] >= 7.0f) : (v[k] <= -7.0f);
-        const float g = ill ? INFINITY : fmaf(fabsf(m[k]), -2.0f * dd[k], d2c[k]);
+        const float g = ill ? INFINITY : __fadd_rn(__fmul_rn(fabsf(m[k]), -2.0f * dd[k]), d2c[k]);
         if (g < best) { best = g; bi = (int)c; }
       }
     }
@@ -901,7 +906,7 @@ __global__ void __launch_bounds__(1024) refine_rows_kernel(float *M, float *v4, 
 #pragma unroll
     for (int k = 0; k < RC; k++) {
       const int64_t c = (int64_t)k * nthr + t;
-      if (c < C) m[k] = fmaf(coef, __ldg(gr + c), m[k]);
+      if (c < C) m[k] = __fadd_rn(m[k], __fmul_rn(coef, __ldg(gr + c)));
     }
     nflip++;
     __syncthreads();
@@ -1005,7 +1010,10 @@ static int gemm_simt_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float a
 }
 
 // Lower Cholesky in place of the n x n block at A (row-major, leading dim
-// ld), blocked right-looking with 64-wide panels.
+// ld), blocked right-looking with 64-wide panels.  Used only by the
+// allocation-free entry point: its products call the SIMT GEMM directly, never
+// the tensor-core path (which allocates its split operands), whatever the
+// dispatch thresholds are.
 static int potrf_lower_ld(float *A, int64_t n, int64_t ld, int *info_dev, cudaStream_t s) {
   for (int64_t k = 0; k < n; k += CB) {
     const int b = (int)std::min<int64_t>(CB, n - k);
@@ -1015,7 +1023,8 @@ static int potrf_lower_ld(float *A, int64_t n, int64_t ld, int *info_dev, cudaSt
       trsm_panel_kernel<<<nblk(rest, 128), 128, 0, s>>>(A, ld, n, k, b);
       // trailing update A22 -= P P^T  (P = A[k+b:, k:k+b])
       const float *P = A + (k + b) * ld + k;
-      int st = hif4x_gemm(0, 1, rest, rest, b, -1.0f, P, ld, 0, P, ld, 0, 1.0f, A + (k + b) * ld + (k + b), ld, 0, 1, s);
+      int st = gemm_simt_ex(0, 1, rest, rest, b, -1.0f, P, ld, 0, P, ld, 0, 1.0f, A + (k + b) * ld + (k + b), ld, 0,
+                            1, 0, s);
       if (st) return st;
     }
   }
@@ -1065,6 +1074,7 @@ static int potrf_inv_rec(float *A, int64_t n, int64_t ld, float *Inv, int64_t ld
 
 // In-place inverse of a lower-triangular n x n block at A (leading dim ld):
 // inv([[A11, 0], [A21, A22]]) = [[A11^-1, 0], [-A22^-1 A21 A11^-1, A22^-1]].
+// Allocation-free entry point only; SIMT products, as potrf_lower_ld.
 static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_t s) {
   if (n <= PB) return potrf_inv128(A, ld, (int)n, A, ld, nullptr, 2, s);
   int64_t n1 = ((n / 2 + PB - 1) / PB) * PB;
@@ -1075,9 +1085,9 @@ static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_
   st = trtri_lower(A22, n2, ld, work, s);
   if (st) return st;
   // T = A21 * A11^-1  (n2 x n1) into work; A21 = -A22^-1 * T
-  st = hif4x_gemm(0, 0, n2, n1, n1, 1.0f, A21, ld, 0, A11, ld, 0, 0.0f, work, n1, 0, 1, s);
+  st = gemm_simt_ex(0, 0, n2, n1, n1, 1.0f, A21, ld, 0, A11, ld, 0, 0.0f, work, n1, 0, 1, 0, s);
   if (st) return st;
-  return hif4x_gemm(0, 0, n2, n1, n2, -1.0f, A22, ld, 0, work, n1, 0, 0.0f, A21, ld, 0, 1, s);
+  return gemm_simt_ex(0, 0, n2, n1, n2, -1.0f, A22, ld, 0, work, n1, 0, 0.0f, A21, ld, 0, 1, 0, s);
 }
 
 extern "C" int hif4x_chol_upper_inv_async(const float *H, int64_t n, int64_t batch, float damp, float *U,
@@ -1193,15 +1203,22 @@ extern "C" int hif4x_refine_rows(float *M, float *v4, const float *d, const floa
 // Host code cannot pass the array's name to a kernel (in host code that name
 // is a host-side stand-in, not a device address), so the first call on each
 // device resolves the device address with cudaGetSymbolAddress while that
-// device is current and caches it; make that first call before any stream
-// capture.  All calls share the one array: calls that overlap on the GPU
-// (different streams or host threads at once) race on it.
+// device is current and caches it per device ordinal (the runtime's primary
+// context of that device; a caller that makes another driver context current
+// must not use this entry point).  Every call ends by copying the pivot flag
+// to the host and synchronising its stream, so no call can be part of a
+// stream capture.  All calls share the one array: calls that overlap on the
+// GPU (different streams or host threads at once) race on it.  It computes the
+// same factor as hif4x_chol_upper_inv in a different order (blocked Cholesky,
+// then a triangular inverse), so the two agree to float rounding, not bit for
+// bit.
 #include <mutex>
 
 namespace {
 constexpr int64_t kNoAllocMaxN = 512;
 constexpr int kNoAllocMaxDevices = 64;
 // [0, n*n): index-reversed damped matrix, later L and L^-1; [n*n, 2*n*n): trtri work
+// (its largest product needs n2*n1 <= n*n/4 floats)
 static __device__ __align__(256) float g_chol_noalloc_scratch[2 * kNoAllocMaxN * kNoAllocMaxN];
 // [0]: non-positive-pivot flag (cleared at the start of every call)
 static __device__ __align__(256) int g_chol_noalloc_info[64];

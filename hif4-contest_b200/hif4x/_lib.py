@@ -86,6 +86,7 @@ SIGNATURES: dict[str, list] = {
     "hif4x_chol_upper_inv_noalloc": [vp, i64, i64, f32, vp, vp],
     "hif4x_gemm_tc": [i32, i32, i64, i64, i64, f32, vp, i64, vp, i64, f32, vp, i64, vp],
     "hif4x_device_status": [vp],
+    "hif4x_wait_selftest": [ctypes.c_longlong, vp, vp],
     "hif4x_gemm_simt": [i32, i32, i64, i64, i64, f32, vp, i64, i64, vp, i64, i64, f32, vp, i64, i64, i64, vp],
     "hif4x_gemm_f64": [i32, i32, i32, i32, i64, i64, i64, ctypes.c_double, vp, i64, i64, vp, i64, i64,
                        ctypes.c_double, vp, i64, i64, i64, i32, vp],

@@ -192,8 +192,17 @@ int hif4x_gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, 
                   const float *B, int64_t ldb, float beta, float *C, int64_t ldc, void *stream);
 
 /* Synchronises the stream; returns (and clears) the sticky device status:
- * HIF4X_TIMEOUT if a bounded device-side wait expired since the last call. */
+ * HIF4X_TIMEOUT if a bounded device-side wait expired since the last call.
+ * One status word per device (not per stream): a read clears it for every
+ * stream of that device. */
 int hif4x_device_status(void *stream);
+
+/* Failure-path check of the bounded device-side wait (no counterpart in the
+ * reference, which has no device code): one thread waits `spins` polls
+ * (1 .. 2^22) on an mbarrier that nothing arrives on, with no copy or MMA in
+ * flight, and gives up; *done_dev becomes 2 and the device status then reads
+ * HIF4X_TIMEOUT.  Synchronises the stream. */
+int hif4x_wait_selftest(long long spins, int *done_dev, void *stream);
 
 /* _upper_cholesky_inv (example/solution/solution.py:287-300): U upper with
  * U^T U = (H + damp * max(mean(diag H), 1e-30) I)^-1, for `batch` n x n
@@ -220,10 +229,14 @@ int hif4x_chol_upper_inv_async(const float *H, int64_t n, int64_t batch, float d
  * device array of 2*512*512 floats (2 MiB, held by every GPU that loads the
  * library until exit), so n <= 512; larger n returns HIF4X_ERR_SCRATCH.
  * The first call on a device, with that device current, looks up the array's
- * device address (cudaGetSymbolAddress) and caches it: make that first call
- * before any stream capture.  All calls share the one array and each call
- * clears the pivot flag it needs; calls that overlap on the GPU race.  Same
- * results and status codes as hif4x_chol_upper_inv; synchronises the stream. */
+ * device address (cudaGetSymbolAddress) and caches it per device ordinal, for
+ * the runtime's primary context of that device.  Every call copies its pivot
+ * flag to the host and synchronises `stream`, so it can never run inside a
+ * stream capture.  All calls share the one array and each call clears the
+ * pivot flag it needs; calls that overlap on the GPU race.  Its products run
+ * on the SIMT GEMM only (the tensor-core path allocates).  The same factor as
+ * hif4x_chol_upper_inv up to float rounding (blocked Cholesky then triangular
+ * inverse, not the recursion), with the same status codes. */
 int hif4x_chol_upper_inv_noalloc(const float *H, int64_t n, int64_t batch, float damp, float *U, void *stream);
 
 /* _gptq_quantize_values / _gptq_quantize_batched (example/solution/

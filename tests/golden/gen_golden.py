@@ -2,7 +2,7 @@
 
 Run in a container that holds the reference project (read-only is fine):
 
-    python tests/golden/gen_golden.py --ref /root/reference
+    python tests/golden/gen_golden.py --ref <reference checkout>
 
 It imports the reference's own modules in-process -- example/solution/
 solution.py (the drop-in solution), dev/variants.py (quant_alg1, the
@@ -104,7 +104,7 @@ def encode_edge_inputs(seed: int) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository")
     args = ap.parse_args()
     sol, variants, ref_hif4 = load_ref(args.ref)
     torch.set_num_threads(8)

@@ -8,7 +8,7 @@ in tests/golden/pipeline_golden.npz:
     output on the NVFP4-decoded inputs (linear: X W^T; attention:
     softmax(QK^T/sqrt(dh))V), for the reference and for Algorithm 1.
 
-    python tests/golden/gen_pipeline_golden.py --ref /root/reference
+    python tests/golden/gen_pipeline_golden.py --ref <reference checkout>
 """
 from __future__ import annotations
 
@@ -44,7 +44,7 @@ def packed(p: dict, rows=None):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository")
     ap.add_argument("--only", nargs="*", help="regenerate these cases, keep the rest of the file")
     args = ap.parse_args()
     sol = load_solution(args.ref)
@@ -53,7 +53,7 @@ def main():
     path = os.path.join(HERE, "pipeline_golden.npz")
     if args.only:
         out = {k: v for k, v in np.load(path).items() if k.split("/")[0] not in args.only}
-    for name in pc.LINEAR_CASES:
+    for name in list(pc.LINEAR_CASES) + list(pc.LAYER_CASES):
         if args.only and name not in args.only:
             continue
         wpair, calib, tests, digest = pc.linear_inputs(name)
@@ -67,7 +67,7 @@ def main():
         out[f"{name}/has_gw"] = np.int64(st["gw"] is not None)
         out[f"{name}/s"] = st["s"].numpy()
         out[f"{name}/order"] = st["order"].numpy() if st["order"] is not None else np.zeros(0, np.int64)
-        wrows = pc.code_rows(wpair[0].shape[0])
+        wrows = pc.code_rows(*wpair[0].shape)
         meta, codes = packed(res["weight_params"], wrows)
         out[f"{name}/w_meta"], out[f"{name}/w_codes"] = meta, codes
         W = pc.deq_nvfp4(wpair)
@@ -83,15 +83,16 @@ def main():
             out[f"{name}/t{i}/mse"] = np.float64(((Yq - Y) ** 2).mean())
             out[f"{name}/t{i}/mse_std"] = np.float64(((Ya - Y) ** 2).mean())
             out[f"{name}/t{i}/ref_power"] = np.float64((Y ** 2).mean())
-            m, c = packed(pa, pc.code_rows(tp[0].shape[0]))
+            m, c = packed(pa, pc.code_rows(*tp[0].shape))
             out[f"{name}/t{i}/meta"], out[f"{name}/t{i}/codes"] = m, c
         print(name, "done in", round(time.time() - t0, 1), "s; mode", st["mode"], "g", st["g"], "tmax", st["tmax"],
               "score", [round(1 - out[f"{name}/t{i}/mse"] / out[f"{name}/t{i}/mse_std"], 4) for i in range(len(tests))])
 
-    for name in pc.ATTN_CASES:
+    for name in list(pc.ATTN_CASES) + list(pc.ATTN_C3_CASES):
         if args.only and name not in args.only:
             continue
         (qh, kvh, dh), calib, tests, digest = pc.attn_inputs(name)
+        t0 = time.time()
         res = sol.hif4_calibration_attention(calib, qh, kvh, dh)
         out[f"{name}/digest"] = np.frombuffer(bytes.fromhex(digest), np.uint8)
         qs, ks = res["q_state"], res["k_state"]
@@ -112,9 +113,9 @@ def main():
             out[f"{name}/t{i}/mse_std"] = np.float64(((oa - ref) ** 2).mean())
             out[f"{name}/t{i}/ref_power"] = np.float64((ref ** 2).mean())
             for role, p in (("q", pq), ("k", pk), ("v", pv)):
-                m, c = packed(p)
+                m, c = packed(p, pc.code_rows(*smp[role][0].shape))
                 out[f"{name}/t{i}/{role}_meta"], out[f"{name}/t{i}/{role}_codes"] = m, c
-        print(name, "rot", qs["rot"], "gq", qs.get("gq", 0),
+        print(name, "done in", round(time.time() - t0, 1), "s; rot", qs["rot"], "gq", qs.get("gq", 0),
               "score", [round(1 - out[f"{name}/t{i}/mse"] / out[f"{name}/t{i}/mse_std"], 4) for i in range(len(tests))])
     for name in pc.EDGE_LINEAR_CASES:
         if args.only and name not in args.only:
@@ -171,7 +172,7 @@ def main():
             out[f"{name}/t{i}/mse_std"] = np.float64(((oa - ref) ** 2).mean())
             out[f"{name}/t{i}/ref_power"] = np.float64((ref ** 2).mean())
             for role, p in (("q", pq), ("k", pk), ("v", pv)):
-                m, c = packed(p, pc.code_rows(smp[role][0].shape[0]))
+                m, c = packed(p, pc.code_rows(*smp[role][0].shape))
                 out[f"{name}/t{i}/{role}_meta"], out[f"{name}/t{i}/{role}_codes"] = m, c
             print(f"  {name}/t{i} T={smp['q'][0].shape[0]} vcomp {sol._VCOMP['n']} qkv {dt:.2f} s")
         print(name, "rot", qs["rot"], "gq", qs.get("gq", 0),

@@ -7,7 +7,7 @@ generator), so only V* is stored.  The reference's batched float64
 torch.linalg.solve stops with an MKL DLASWP parameter error and never returns
 when MKL runs 8 threads on the build host; it runs on one thread here.
 
-    python tests/golden/gen_vcomp_golden.py --ref /root/reference
+    python tests/golden/gen_vcomp_golden.py --ref <reference checkout>
 """
 from __future__ import annotations
 
@@ -42,7 +42,7 @@ def vcomp_inputs(name: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository")
     args = ap.parse_args()
     spec = importlib.util.spec_from_file_location("ref_solution", os.path.join(args.ref, "example", "solution",
                                                                                "solution.py"))

@@ -83,3 +83,22 @@ def test_tc_gemm_unaligned_leading_dims():
     ref = A.double() @ B.double()
     assert float((C.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * K ** 0.5 + 1e-6
     assert float(Cbig[:, 0].abs().max()) == 0.0 and float(Cbig[:, 258:].abs().max()) == 0.0
+
+
+def test_bounded_wait_runs_out_and_reports_timeout():
+    """The failure path of the kernels' bounded mbarrier waits: a wait that
+    nothing completes (no copy or MMA in flight) gives up after its spin
+    limit, the device status reads TIMEOUT once and is then cleared, and the
+    context stays usable -- a tensor-core GEMM afterwards is correct."""
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    done = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert L.lib().hif4x_wait_selftest(1000, L.ptr(done), L.stream()) == L.OK
+    assert int(done.item()) == 2
+    assert L.lib().hif4x_device_status(L.stream()) == L.TIMEOUT
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    assert L.lib().hif4x_wait_selftest(0, L.ptr(done), L.stream()) == L.ERR_ARG
+    A, B = rnd(512, 256, seed=11), rnd(512, 256, seed=12)
+    got = tc_gemm(A, B, 0, 1)
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    ref = A.double() @ B.double().T
+    assert float((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * 256 ** 0.5 + 1e-6
