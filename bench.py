@@ -278,10 +278,20 @@ def run_gpu(args, rank, ws, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, k_ms = float(t[0]), float(t[1])
 
-    e2e = None
+    e2e = e2e_api = None
     if not args.no_e2e:
         e2e = e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dist)
+        e2e_api = e2e_api_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, barrier, dist)
     clk.stop()
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_oracle_sample(codes, e4m3, s_dec, CPU_SAMPLE_ROWS)
+    pipeline = None
+    if not args.no_pipeline:
+        del codes, e4m3, meta, hcodes, rt
+        torch.cuda.empty_cache()
+        pipeline = weightset_bench(rank, ws, local_rank, args.pipeline_layers, 8192, 4, 1024, args.pipeline_steps,
+                                   args.pipeline_warmup, args.workers)
     if rank != 0:
         return
     elems = ROWS * COLS
@@ -305,12 +315,26 @@ def run_gpu(args, rank, ws, local_rank):
     if e2e is not None:
         e2e_ms, launches_e2e, h2d, d2h = e2e
         line["e2e"] = {"value": ws * elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": h2d,
-                       "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "gpu_launches": launches_e2e}
-    if ws == 1 and not args.no_cpu_baseline:
-        v, n, dt = cpu_oracle_sample(codes, e4m3, s_dec, CPU_SAMPLE_ROWS)
+                       "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "gpu_launches": launches_e2e,
+                       "form": "packed NVFP4 host buffers in (0.5625 B/elem), packed HiF4 host buffers out "
+                               "(0.5625 B/elem), hif4x.api.PackedConverter"}
+    if e2e_api is not None:
+        api_ms, launches_api, h2d, d2h = e2e_api
+        line["e2e_api"] = {"value": ws * elems / (api_ms * 1e-3) / 1e9, "unit": "Gelem/s",
+                           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": api_ms,
+                           "gpu_launches": launches_api,
+                           "form": "the reference API's form: host NVFP4 pair (bf16 carrier + fp32 scale, "
+                                   "2.25 B/elem) in, host dict5 fp32 (9.5625 B/elem) out, "
+                                   "hif4x.api.PairConverter"}
+    if cpu is not None:
+        v, n, dt = cpu
         line["cpu_baseline"] = {"value": v / 1e9, "unit": "Gelem/s", "cores": n, "kind": "port",
                                 "sample": f"first {CPU_SAMPLE_ROWS} of {ROWS} rows of the same tensor "
                                           f"({dt:.1f} s, oracle C port of the reference codec, OpenMP)"}
+    if pipeline is not None:
+        line["pipeline"] = {"metric": "NVFP4->HiF4 weight-set conversion (full calibration: smoothing, rotation "
+                                      "choice, GPTQ, refinement, Gram carries; one 1024-token dynamic call per "
+                                      "matrix)", **pipeline}
     print(json.dumps(line), flush=True)
 
 
@@ -347,13 +371,17 @@ def e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dis
     return e2e_ms, launches_e2e, int(codes_h.numel() + e4m3_h.numel()), int(meta_h.numel() * 4 + hcodes_h.numel())
 
 
-def run_layer(args, rank, ws, local_rank):
-    """Pipeline workload: Llama-3-8B-shaped decoder layers (7 matrices each),
-    full calibration (smoothing, rotation choice, GPTQ, refinement, Gram
-    carries) plus one 1024-token dynamic activation call per matrix, through
-    the public API with CPU tensors.  Whole matrices are sharded over the
-    ranks by LPT; the packed HiF4 weights are gathered to rank 0 (NCCL).
-    value = matrices/s over all ranks (fixed total work: strong scaling)."""
+def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, warmup, workers,
+                    api_legs=False):
+    """Pipeline workload: `layers` Llama-3-8B-shaped decoder layers (7 matrices
+    each), full calibration (smoothing, rotation choice, GPTQ, refinement,
+    Gram carries) plus one T_test-token dynamic activation call per matrix.
+    Whole matrices are sharded over the ranks by LPT; each rank packs its
+    converted weights on the device and the packed HiF4 (4.5 bit/elem) goes to
+    rank 0 by NCCL point-to-point inside the timed step.  Inputs are generated
+    on the device (N(0, 0.02) weights; T_cal calibration tokens per layer
+    input in n_cal samples, 0.2 % of the channels x20, the down_proj input
+    |N|*SiLU-shaped).  Returns the measurements on rank 0, None elsewhere."""
     import torch
 
     from hif4x import codec, linear, score, shard, synth, weightset
@@ -362,14 +390,11 @@ def run_layer(args, rank, ws, local_rank):
     dist = None
     if ws > 1:
         import torch.distributed as dist
-    T_cal, n_cal, T_test = 4096, 4, 1024
-    jobs = shard.model_jobs(args.layers)
+    jobs = shard.model_jobs(layers)
     mine = shard.rank_jobs(jobs, rank, ws, T_cal)
 
     def pair(x):
-        return [t.cpu() for t in synth.reference_form(*synth.quantize_nvfp4(x))]
-
-    inputs = {}
+        return list(synth.reference_form(*synth.quantize_nvfp4(x)))
 
     def acts(layer, input_id, C, seed_off, T):
         seed = 10_000 * layer + zlib.crc32(input_id.encode()) % 997 * 10 + seed_off
@@ -377,48 +402,51 @@ def run_layer(args, rank, ws, local_rank):
             return synth.acts_silu(seed, T, C, device=dev)
         return synth.acts_outlier(seed, T, C, n_out=max(1, round(C * 0.002)), gain=20.0, device=dev)
 
+    dev_inputs, dev_weights = {}, {}
     for j in mine:
         key = (j.layer, j.input_id)
-        if key not in inputs:
-            inputs[key] = ([pair(acts(j.layer, j.input_id, j.C, i, T_cal // n_cal)) for i in range(n_cal)],
-                           pair(acts(j.layer, j.input_id, j.C, 99, T_test)))
-    weights = {j.key: pair((torch.randn(j.N, j.C, device=dev,
-                                        generator=torch.Generator(device=dev).manual_seed(zlib.crc32(j.key.encode())))
-                            * 0.02).to(torch.bfloat16)) for j in mine}
-    # device-resident copies of the same inputs
-    to_dev = lambda pr: [t.to(dev) for t in pr]  # noqa: E731
-    dev_x = score.decode_pair
-    dev_inputs = {k: ([to_dev(c) for c in cal], to_dev(tst)) for k, (cal, tst) in inputs.items()}
-    dev_weights = {k: to_dev(v) for k, v in weights.items()}
+        if key not in dev_inputs:
+            dev_inputs[key] = ([pair(acts(j.layer, j.input_id, j.C, i, T_cal // n_cal)) for i in range(n_cal)],
+                               pair(acts(j.layer, j.input_id, j.C, 99, T_test)))
+        g = torch.Generator(device=dev).manual_seed(zlib.crc32(j.key.encode()))
+        dev_weights[j.key] = pair((torch.randn(j.N, j.C, device=dev, generator=g) * 0.02).to(torch.bfloat16))
+    # CPU copies of the same inputs for the six-function API legs
+    to_cpu = lambda pr: [t.cpu() for t in pr]  # noqa: E731
+    inputs = {k: ([to_cpu(c) for c in cal], to_cpu(tst)) for k, (cal, tst) in dev_inputs.items()} if api_legs else {}
+    weights = {k: to_cpu(v) for k, v in dev_weights.items()} if api_legs else {}
     torch.cuda.synchronize(dev)
 
-    packed = {}
-    outputs = {}
+    packed, outputs, shards = {}, {}, {}
+    compact_api = [False]
 
     def step(device_resident: bool):
         if device_resident:
-            # independent matrices concurrently on `workers` streams
-            # longest first (the cost model), so the long matrices do not finish last
+            # longest first (the cost model), so the long matrices do not finish last;
+            # the matrices within half of the longest one's cost on high-priority streams
             order = sorted(mine, key=lambda j: -shard.matrix_cost(j.N, j.C, T_cal))
             todo = [(j.key, dev_weights[j.key], dev_inputs[(j.layer, j.input_id)][0],
                      dev_inputs[(j.layer, j.input_id)][1]) for j in order]
-            # each matrix packed as it finishes; its dict5 and states are dropped
-            # the matrices within half of the longest one's cost run on high-priority streams
             top = shard.matrix_cost(order[0].N, order[0].C, T_cal) if order else 0.0
             urgent = {j.key for j in order if shard.matrix_cost(j.N, j.C, T_cal) >= 0.5 * top}
-            done = weightset.convert(todo, workers=args.workers, device=dev, urgent=urgent,
+            # each matrix packed on its worker's stream as it finishes; its dict5 and states are dropped
+            done = weightset.convert(todo, workers=workers, device=dev, urgent=urgent,
                                      consume=lambda key, res, dyn: (shard.pack_params(res["weight_params"]),
                                                                     codec.pack(dyn)))
             for key, (buf, dyn) in done.items():
                 packed[key] = buf
                 outputs[key] = dyn
-            return
-        for j in mine:   # the six-function API, one matrix after another, CPU tensors
-            calib, test = inputs[(j.layer, j.input_id)]
-            wq, wsc = weights[j.key]
-            res = linear.calibrate_weight(wq, wsc, calib, compact=compact_api)
-            linear.dynamic_activation(test[0], test[1], res["activation_state"])
-            packed[j.key] = shard.pack_params(res["weight_params"])
+        else:
+            for j in mine:   # the six-function API, one matrix after another, CPU tensors
+                calib, test = inputs[(j.layer, j.input_id)]
+                wq, wsc = weights[j.key]
+                res = linear.calibrate_weight(wq, wsc, calib, compact=compact_api[0])
+                linear.dynamic_activation(test[0], test[1], res["activation_state"])
+                packed[j.key] = shard.pack_params(res["weight_params"])
+        # the converted weights, packed, to rank 0 (NCCL send/recv)
+        got = shard.gather_shards(packed, dist, dev) if dist is not None else dict(packed)
+        shards.clear()
+        if got is not None:
+            shards.update(got)
 
     def barrier():
         if dist is not None:
@@ -429,37 +457,38 @@ def run_layer(args, rank, ws, local_rank):
     window = {}
 
     def timed(device_resident: bool) -> float:
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             step(device_resident)
         torch.cuda.synchronize(dev)
         barrier()
-        # CUDA events on the stream every kernel of the step is launched on
-        # (the step's worker streams join it before the step returns)
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        # CUDA events on the current stream: the step's worker streams and the
+        # gather join it before the step returns
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
         w0 = time.time()
         evs[0].record()
-        for k in range(args.steps):
+        for k in range(steps):
             step(device_resident)
             evs[k + 1].record()
         torch.cuda.synchronize(dev)
         if device_resident:
             window["w"] = (w0, time.time())
-            window["step_ms"] = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
-        dt = evs[0].elapsed_time(evs[-1]) / 1e3 / max(args.steps, 1)
+            window["step_ms"] = [evs[k].elapsed_time(evs[k + 1]) for k in range(steps)]
+        dt = evs[0].elapsed_time(evs[-1]) / 1e3 / max(steps, 1)
         if dist is not None:
             t = torch.tensor([dt], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             dt = float(t[0])
         return dt
 
-    compact_api = False
     dt = timed(True)
     clk.stop()
     dev_packed = dict(packed)   # the device-resident run's weights, for the quality below
+    digest = shard.checksum(shards) if rank == 0 else None
+    gathered = len(shards)
     dt_api = dt_api_compact = None
-    if not args.no_e2e:
+    if api_legs:
         dt_api = timed(False)
-        compact_api = True
+        compact_api[0] = True
         dt_api_compact = timed(False)
     # contest quality of this rank's matrices (the device-resident run's
     # outputs): output MSE of the test activations through the converted
@@ -469,7 +498,8 @@ def run_layer(args, rank, ws, local_rank):
     for j in mine:
         x_hat = codec.decode_packed(*outputs[j.key], torch.float32)
         w_hat = codec.decode_packed(*shard.unpack_params(dev_packed[j.key], j.N, j.C), torch.float32)
-        sc = score.linear(dev_x(dev_inputs[(j.layer, j.input_id)][1]), dev_x(dev_weights[j.key]), x_hat, w_hat)
+        sc = score.linear(score.decode_pair(dev_inputs[(j.layer, j.input_id)][1]),
+                          score.decode_pair(dev_weights[j.key]), x_hat, w_hat)
         q[0] += sc["rel_mse"]
         q[1] += sc["score"]
         q[2] += 1
@@ -479,39 +509,89 @@ def run_layer(args, rank, ws, local_rank):
         dist.all_reduce(q, op=dist.ReduceOp.SUM)
         dist.all_reduce(qm, op=dist.ReduceOp.MAX)
         q[3] = qm[0]
-    if dist is not None:
-        g0 = time.perf_counter()
-        shards = shard.gather_shards(packed, dist, dev)
-        torch.cuda.synchronize(dev)
-        gather_s = time.perf_counter() - g0
-    else:
-        shards, gather_s = packed, 0.0
     if rank != 0:
-        return
+        return None
+    assert gathered == len(jobs), (gathered, len(jobs))
     elems = sum(j.N * j.C for j in jobs)
-    assert shards is not None and len(shards) == len(jobs)
-    print(json.dumps({
-        "metric": "NVFP4->HiF4 weight-set conversion, matrices/s (full calibration + one dynamic call each)",
-        "value": len(jobs) / dt, "unit": "matrices/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.layers} Llama-3-8B-shaped decoder layer(s), {len(jobs)} matrices, "
-                               f"{T_cal} calibration tokens per input ({n_cal} x {T_cal // n_cal}), 1 x {T_test} "
-                               "dynamic tokens per matrix",
-                   "parallelism": f"LPT over {ws} GPU(s), {args.workers} concurrent matrices per GPU"},
-        "weight_gelem_per_s": elems / dt / 1e9, "gather_s": gather_s,
-        "step_ms_rank0": window["step_ms"], "clocks": clk.summary(*window["w"]),
+    return {
+        "value": len(jobs) / dt, "unit": "matrices/s", "weight_gelem_per_s": elems / dt / 1e9,
+        "n_gpus": ws, "steps": steps, "warmup": warmup, "ms_per_step": dt * 1e3,
+        "step_ms_rank0": window["step_ms"], "scaling": "strong", "matrices": len(jobs),
+        "weight_elements": elems, "clocks": clk.summary(*window["w"]),
+        "gathered_bytes": int(sum(int(b.numel()) for b in shards.values())),
+        "packed_checksum": digest,
         "quality": {"mean_rel_output_mse": float(q[0] / q[2]), "max_rel_output_mse": float(q[3]),
                     "mean_score_vs_alg1": float(q[1] / q[2]), "matrices": int(q[2]),
-                    "note": "|X W^T - X^ W^^T|^2 / |X W^T|^2 on each matrix's 1024-token test input; "
+                    "note": f"|X W^T - X^ W^^T|^2 / |X W^T|^2 on each matrix's {T_test}-token test input; "
                             "score = (MSE_alg1 - MSE) / MSE_alg1 (the contest's rule)"},
-        "e2e": None if dt_api is None else {
+        "api": None if dt_api is None else {
             "value": len(jobs) / dt_api, "unit": "matrices/s", "ms_per_step": dt_api * 1e3,
             "note": "through the six-function API: CPU tensors in, CPU dict5 and CPU states out",
             "compact_state": {"value": len(jobs) / dt_api_compact, "unit": "matrices/s",
                               "ms_per_step": dt_api_compact * 1e3}},
-        "timing_note": "CUDA events on the launching stream around the timed steps, max over ranks",
-    }), flush=True)
+        "config": {"workload": f"{layers} Llama-3-8B-shaped decoder layer(s), {len(jobs)} matrices, "
+                               f"{T_cal} calibration tokens per layer input ({n_cal} x {T_cal // n_cal}), "
+                               f"1 x {T_test} dynamic tokens per matrix",
+                   "parallelism": f"LPT over {ws} GPU(s), {workers} concurrent matrices per GPU; packed "
+                                  "HiF4 gathered to rank 0 (NCCL send/recv) inside the timed step"},
+        "timing_note": "CUDA events on the launching stream around the timed steps (worker streams and the "
+                       "gather joined before each step ends), max over ranks",
+    }
+
+
+def e2e_api_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, barrier, dist):
+    """The codec in the reference API's form through the GPU: the host NVFP4
+    pair (bf16 carrier + fp32 scale) in and the host dict5 (five fp32 arrays)
+    out, every copy inside the timed region; the first rows are checked
+    against the device-resident run's packed output."""
+    import torch
+
+    from hif4x import codec, synth
+    from hif4x.api import PairConverter
+    carrier, scale = synth.reference_form(codes, e4m3, s_dec)
+    carrier_h, scale_h = carrier.cpu().pin_memory(), scale.cpu().pin_memory()
+    del carrier, scale
+    out_h = PairConverter.empty_host(ROWS, COLS)
+    conv = PairConverter(ROWS, COLS, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(2, args.warmup)):
+        conv(carrier_h, scale_h, out_h)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    launches = 0
+    for _ in range(K):
+        launches += conv(carrier_h, scale_h, out_h)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = e0.elapsed_time(e1) / K
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    n = 256
+    p = codec.Dict5(*(out_h[k][:n].to(dev) for k in PairConverter.OUTS))
+    m, c = codec.pack(p)
+    assert torch.equal(m, meta[:n]) and torch.equal(c, hcodes[:n]), "dict5 output differs from the packed run"
+    h2d = carrier_h.numel() * 2 + scale_h.numel() * 4
+    d2h = sum(t.numel() * 4 for t in out_h.values())
+    del out_h, carrier_h, scale_h, conv
+    return ms, launches, h2d, d2h
+
+
+def run_layer(args, rank, ws, local_rank):
+    """--workload layer: the weight-set pipeline alone, with the API legs."""
+    res = weightset_bench(rank, ws, local_rank, args.layers, 4096, 4, 1024, args.steps, args.warmup, args.workers,
+                          api_legs=not args.no_e2e)
+    if rank != 0:
+        return
+    api = res.pop("api")
+    line = {"metric": "NVFP4->HiF4 weight-set conversion, matrices/s (full calibration + one dynamic call each)",
+            "higher_is_better": True, "vs_baseline": None, "dtype": "f32", "data": "synthetic", **res}
+    line["e2e"] = api
+    print(json.dumps(line), flush=True)
 
 
 def run_attention(args, rank, ws, local_rank):
@@ -623,6 +703,11 @@ def main():
     ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention"])
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
     ap.add_argument("--workers", type=int, default=3, help="layer workload: matrices in flight per GPU")
+    ap.add_argument("--no-pipeline", action="store_true", help="codec workload: skip the weight-set object")
+    ap.add_argument("--pipeline-layers", type=int, default=32,
+                    help="codec workload: decoder layers of the weight-set object (32 = the full weight set)")
+    ap.add_argument("--pipeline-steps", type=int, default=2, help="timed conversions of the weight set")
+    ap.add_argument("--pipeline-warmup", type=int, default=1, help="untimed conversions of the weight set first")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "codec":
         args.warmup = 3

@@ -137,6 +137,95 @@ class PackedConverter:
         return n
 
 
+class PairConverter:
+    """The reference API's own form through the GPU: NVFP4 as the host pair
+    [carrier (R, C) bf16, scale (R, C/16) fp32] in (2.25 B/elem), HiF4 as host
+    dict5 fp32 arrays out (9.5625 B/elem): sf (R, C/64), lv2 (R, C/64, 8),
+    lv3 (R, C/64, 16), sign (R, C), mant (R, C) -- the reference's
+    scale_factor / scale_lv2 / scale_lv3 / sign / mant (self_check.py:75-95)
+    up to a reshape.  Chunks of rows stream through the same three-stream
+    pipeline as PackedConverter (upload, fused decode -> rot64 -> searched
+    encode, download), so the time approaches the 11.8 B/elem of PCIe traffic.
+    Host tensors should be pinned."""
+
+    OUTS = ("sf", "lv2", "lv3", "sign", "mant")
+
+    def __init__(self, rows: int, cols: int, *, chunk_rows: int = 1024, nbuf: int = 3, device=None,
+                 rotate: bool = True):
+        self.R, self.C = rows, cols
+        self.dev = torch.device(device or torch.cuda.current_device())
+        self.chunk = min(chunk_rows, rows)
+        self.s_h2d, self.s_comp, self.s_d2h = (torch.cuda.Stream(self.dev) for _ in range(3))
+        c, f, nb = self.chunk, cols, cols // 64
+        dv = dict(device=self.dev)
+        self.bufs = []
+        for _ in range(max(2, nbuf)):
+            self.bufs.append({
+                "carrier": torch.empty(c, f, dtype=torch.bfloat16, **dv),
+                "scale": torch.empty(c, f // 16, dtype=torch.float32, **dv),
+                "sf": torch.empty(c, nb, dtype=torch.float32, **dv),
+                "lv2": torch.empty(c, nb, 8, dtype=torch.float32, **dv),
+                "lv3": torch.empty(c, nb, 16, dtype=torch.float32, **dv),
+                "sign": torch.empty(c, f, dtype=torch.float32, **dv),
+                "mant": torch.empty(c, f, dtype=torch.float32, **dv),
+                "in_ready": torch.cuda.Event(), "computed": torch.cuda.Event(), "drained": torch.cuda.Event(),
+            })
+        self.signs = codec.rot_signs(cols // 64, self.dev) if rotate else None
+
+    @staticmethod
+    def empty_host(rows: int, cols: int) -> dict:
+        """Pinned host dict5 arrays for one conversion."""
+        nb = cols // 64
+        f = dict(dtype=torch.float32, pin_memory=True)
+        return {"sf": torch.empty(rows, nb, **f), "lv2": torch.empty(rows, nb, 8, **f),
+                "lv3": torch.empty(rows, nb, 16, **f), "sign": torch.empty(rows, cols, **f),
+                "mant": torch.empty(rows, cols, **f)}
+
+    def __call__(self, carrier_h: torch.Tensor, scale_h: torch.Tensor, out_h: dict) -> int:
+        """Convert into out_h (empty_host's arrays); returns kernels launched.
+        Ordered after the current stream's work, and the current stream after it."""
+        R = carrier_h.shape[0]
+        cur = torch.cuda.current_stream(self.dev)
+        for s in (self.s_h2d, self.s_comp, self.s_d2h):
+            s.wait_stream(cur)
+        n, nbuf = 0, len(self.bufs)
+        for k, r0 in enumerate(range(0, R, self.chunk)):
+            r1 = min(R, r0 + self.chunk)
+            rows = r1 - r0
+            b = self.bufs[k % nbuf]
+            reuse = k >= nbuf
+            with torch.cuda.stream(self.s_h2d):
+                if reuse:
+                    self.s_h2d.wait_event(b["computed"])
+                b["carrier"][:rows].copy_(carrier_h[r0:r1], non_blocking=True)
+                b["scale"][:rows].copy_(scale_h[r0:r1], non_blocking=True)
+                b["in_ready"].record(self.s_h2d)
+            with torch.cuda.stream(self.s_comp):
+                self.s_comp.wait_event(b["in_ready"])
+                if reuse:
+                    self.s_comp.wait_event(b["drained"])
+                d = L.ConvertDesc()
+                d.rows, d.cols = rows, self.C
+                d.src_kind, d.src_dtype, d.scale_dtype = L.SRC_NVFP4_PAIR, L.DT_BF16, L.DT_F32
+                d.src, d.src_scale = b["carrier"].data_ptr(), b["scale"].data_ptr()
+                if self.signs is not None:
+                    d.rot_signs = self.signs.data_ptr()
+                d.encode_mode = L.ENC_SEARCH
+                d.sf, d.lv2, d.lv3 = b["sf"].data_ptr(), b["lv2"].data_ptr(), b["lv3"].data_ptr()
+                d.sign, d.mant = b["sign"].data_ptr(), b["mant"].data_ptr()
+                L.call("hif4x_convert", L.ctypes.byref(d), L.vp(self.s_comp.cuda_stream))
+                n += 1
+                b["computed"].record(self.s_comp)
+            with torch.cuda.stream(self.s_d2h):
+                self.s_d2h.wait_event(b["computed"])
+                for name in self.OUTS:
+                    out_h[name][r0:r1].copy_(b[name][:rows], non_blocking=True)
+                b["drained"].record(self.s_d2h)
+        for s in (self.s_h2d, self.s_comp, self.s_d2h):
+            cur.wait_stream(s)
+        return n
+
+
 def split_rows(packed_rows: torch.Tensor, cols: int):
     """(meta (R, C/64) int32, codes (R, C/2) uint8) views of packed HiF4 rows."""
     R = packed_rows.shape[0]

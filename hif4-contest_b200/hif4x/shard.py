@@ -68,12 +68,15 @@ def rank_jobs(jobs: list[MatrixJob], rank: int, world: int, T_cal: int) -> list[
 
 
 def pack_params(p: dict) -> torch.Tensor:
-    """dict5 (CPU, reference shapes) -> one uint8 buffer: packed HiF4 (meta + codes)."""
+    """dict5 (reference shapes) -> one uint8 buffer: packed HiF4 (meta + codes)
+    on the current device.  A CUDA dict5 (calibrate_weight(...,
+    return_device=True)) is packed where it lies, so only the packed 4.5-bit
+    form ever leaves the GPU; a CPU dict5 is uploaded first."""
     from . import codec, hostio
     sf = p["scale_factor"]
     R, nb = sf.shape[0], sf.shape[1]
     C = nb * 64
-    dev = torch.device("cuda", torch.cuda.current_device())
+    dev = sf.device if sf.is_cuda else torch.device("cuda", torch.cuda.current_device())
     up = lambda t, *shape: hostio.to_device(t.reshape(*shape), dev)  # noqa: E731
     d5 = codec.Dict5(up(sf, R, nb), up(p["scale_lv2"], R, nb, 8), up(p["scale_lv3"], R, nb, 16),
                      up(p["sign"], R, C), up(p["mant"], R, C))
@@ -91,27 +94,56 @@ def unpack_params(buf: torch.Tensor, R: int, C: int):
 
 
 def gather_shards(local: dict[str, torch.Tensor], dist, device) -> dict[str, torch.Tensor] | None:
-    """All ranks: contribute {key: uint8 CUDA buffer}; rank 0 receives every
-    rank's buffers (one all_gather of sizes, one of padded payloads, NCCL)."""
-    world = dist.get_world_size()
+    """All ranks: contribute {key: uint8 buffer}; rank 0 receives every other
+    rank's buffers and returns all of them, the others return None.
+
+    The keys and sizes go round as host objects; the payloads travel only to
+    rank 0, one point-to-point message per rank (NCCL send/recv over NVLink
+    on the GPUs), with no padding: rank 0 receives exactly the other ranks'
+    bytes, nothing crosses to the other ranks."""
+    world, rank = dist.get_world_size(), dist.get_rank()
     keys = sorted(local)
-    payload = torch.cat([local[k] for k in keys]) if keys else torch.zeros(0, dtype=torch.uint8, device=device)
-    n = torch.tensor([payload.numel()], dtype=torch.int64, device=device)
-    sizes = [torch.zeros(1, dtype=torch.int64, device=device) for _ in range(world)]
-    dist.all_gather(sizes, n)
-    mx = int(max(int(s.item()) for s in sizes))
-    buf = torch.zeros(mx, dtype=torch.uint8, device=device)
-    buf[:payload.numel()] = payload
-    outs = [torch.empty(mx, dtype=torch.uint8, device=device) for _ in range(world)]
-    dist.all_gather(outs, buf)
     meta = [None] * world
     dist.all_gather_object(meta, [(k, int(local[k].numel())) for k in keys])
-    if dist.get_rank() != 0:
+    if rank != 0:
+        if keys and sum(int(local[k].numel()) for k in keys):
+            payload = torch.cat([local[k].reshape(-1) for k in keys])
+            for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, payload, 0)]):
+                w.wait()
         return None
-    res = {}
-    for r in range(world):
+    res = dict(local)
+    bufs, ops = {}, []
+    for r in range(1, world):
+        n = sum(sz for _, sz in meta[r])
+        if n:
+            bufs[r] = torch.empty(n, dtype=torch.uint8, device=device)
+            ops.append(dist.P2POp(dist.irecv, bufs[r], r))
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    for r, buf in bufs.items():
         off = 0
         for k, sz in meta[r]:
-            res[k] = outs[r][off:off + sz]
+            res[k] = buf[off:off + sz]
             off += sz
     return res
+
+
+def checksum(buffers: dict[str, torch.Tensor]) -> str:
+    """Digest of packed outputs that does not depend on how they were sharded:
+    per buffer a weighted sum of its 32-bit words in int64 (wrapping, so the
+    device's summation order cannot change it), combined in key order.  Equal
+    outputs give equal digests at every GPU count."""
+    acc = 0
+    for k in sorted(buffers):
+        b = buffers[k].reshape(-1)
+        if b.storage_offset() % 4:
+            b = b.clone()
+        pad = (-b.numel()) % 4
+        if pad:
+            b = torch.cat([b, torch.zeros(pad, dtype=torch.uint8, device=b.device)])
+        w = b.view(torch.int32).long()
+        idx = torch.arange(w.numel(), device=w.device, dtype=torch.int64)
+        s = int((w * ((idx * 2654435761) % 2147483647 + 1)).sum())
+        acc = (acc * 1000003 + (s & 0xFFFFFFFFFFFFFFFF) + b.numel()) & 0xFFFFFFFFFFFFFFFF
+    return f"{acc:016x}"

@@ -200,3 +200,66 @@ def test_gptq_row_exchange_identical(R, batch):
         for r0 in (0, R - 64):
             small = la.gptq(x[b, r0:r0 + 64].contiguous(), unit[b, r0:r0 + 64].contiguous(), U[b])
             assert torch.equal(got[b, r0:r0 + 64], small), (b, r0)
+
+
+@pytest.mark.parametrize("n", [4096, 14336])
+def test_chol_upper_inv_production_sizes(n, capsys):
+    """The Cholesky-inverse at the pipeline's sizes (C = 4096: q/k/v/o and
+    gate/up inputs; C = 14336: down_proj), H the Gram of (n + 1024) x n
+    Gaussian rows: U upper, U^T U H_d = I to 1e-3 in float64 (H_d the damped
+    H), and at n = 4096 the float64 CPU oracle's factor to 1e-3 of its
+    largest entry."""
+    X = rnd(n + 1024, n, seed=n + 1)
+    H = la.gemm(X, X, ta=True)
+    del X
+    U = la.chol_upper_inv(H)
+    assert U is not None
+    assert float(torch.tril(U, -1).abs().max()) == 0.0
+    Hd = H.double()
+    Hd.diagonal().add_(max(float(Hd.diagonal().mean()), 1e-30) * 0.1)
+    Ud = U.double()
+    R = Ud.T @ (Ud @ Hd)
+    R.diagonal().sub_(1.0)
+    err = float(R.abs().max())
+    row = float(R.abs().sum(1).max())
+    del R, Hd
+    msg = f"n={n}: max |U^T U H_d - I| = {err:.2e}, max row sum {row:.2e}"
+    if n == 4096:
+        Uref = torch.from_numpy(po.upper_cholesky_inv(H.cpu().numpy())).double()
+        rel = float((Ud.cpu() - Uref).abs().max() / Uref.abs().max())
+        msg += f", vs oracle {rel:.2e}"
+        assert rel < 1e-3
+    with capsys.disabled():
+        print("\n  " + msg)
+    assert err < 1e-3, msg
+
+
+def test_gptq_production_size_vs_oracle(capsys):
+    """GPTQ of a 1024 x 4096 input (a dynamic call's tokens over C = 4096)
+    with a real factor: against the numpy oracle on the same U, the values
+    differ only where the trailing products' rounding (numpy BLAS there,
+    tensor cores here) tips a decision and the error feedback carries it
+    along the row, and the GPTQ objective sum((X - Q) H (X - Q)^T) is the
+    oracle's to 1 %."""
+    R, C = 1024, 4096
+    X = rnd(R, C, seed=31, scale=1.0)
+    A = rnd(C + 1024, C, seed=32)
+    H = la.gemm(A, A, ta=True)
+    del A
+    U = la.chol_upper_inv(H)
+    unit = codec.unit_flat(codec.encode(X))
+    got = la.gptq(X, unit, U)
+    want = torch.from_numpy(po.gptq(X.cpu().numpy(), unit.cpu().numpy(), U.cpu().numpy())).cuda()
+    mism = float((got != want).float().mean())
+    Hd = H.double()
+
+    def objective(Q):
+        E = (X - Q).double()
+        return float(((E @ Hd) * E).sum())
+
+    og, ow = objective(got), objective(want)
+    with capsys.disabled():
+        print(f"\n  gptq {R}x{C}: value mismatch {100 * mism:.2f} %, objective {og:.6e} vs oracle {ow:.6e} "
+              f"({100 * (og / ow - 1):+.3f} %)")
+    assert mism < 0.05
+    assert abs(og / ow - 1) < 0.01

@@ -59,10 +59,10 @@ def check_mse(name, got, want, std, report):
 def check_order(st, gold_order, Wq, report):
     """Act-order (solution.py:936-951) = argsort of the weight Gram's diagonal,
     descending.  The diagonal is a fp32 sum whose rounding depends on the
-    summation order (MKL's there, the tensor cores' here), so columns whose
-    sums differ by a few ulps may swap: at every position where the two
-    orders differ, the two columns' exact (float64) diagonal values must agree
-    to 1e-5 of the largest."""
+    summation order and precision (MKL's fp32 there, the tensor cores'
+    3xTF32 here), so columns whose sums differ in the last few bits may swap:
+    at every position where the two orders differ, the two columns' exact
+    (float64) diagonal values must agree to 1e-4 of the largest."""
     if st["order"] is None:
         assert gold_order.size == 0
         report.append("act-order: none (as the reference)")
@@ -71,9 +71,10 @@ def check_order(st, gold_order, Wq, report):
     assert o.shape == gold_order.shape
     d = (Wq.double() ** 2).sum(0).numpy()
     bad = np.nonzero(o != gold_order)[0]
-    report.append(f"act-order: {o.size - bad.size} of {o.size} positions equal, the rest near-tied")
-    if bad.size:
-        assert np.all(np.abs(d[o[bad]] - d[gold_order[bad]]) <= 1e-5 * d.max()), "act-order differs beyond ties"
+    dev = float(np.abs(d[o[bad]] - d[gold_order[bad]]).max() / d.max()) if bad.size else 0.0
+    report.append(f"act-order: {o.size - bad.size} of {o.size} positions equal; where they differ the "
+                  f"diagonal values agree to {dev:.1e} of the largest")
+    assert dev <= 1e-4, report[-1]
 
 
 @pytest.mark.parametrize("name", list(pc.LINEAR_CASES) + list(pc.LAYER_CASES))

@@ -101,3 +101,20 @@ def _failing_worker(rank, world, port):
         os._exit(3)        # dies between steps, before its collective
     local = {"layers.0.q_proj": torch.zeros(4, dtype=torch.uint8)}
     shard.gather_shards(local, dist, torch.device("cpu"))   # raises: peer gone
+
+
+def test_checksum_ignores_sharding_and_sees_changes():
+    g = torch.Generator().manual_seed(5)
+    bufs = {f"layers.{i}.q_proj": torch.randint(0, 256, (4096 + 4 * i,), generator=g, dtype=torch.uint8)
+            for i in range(6)}
+    whole = shard.checksum(bufs)
+    # the same buffers arriving as slices of one received payload, in another order
+    keys = sorted(bufs)[::-1]
+    payload = torch.cat([bufs[k] for k in keys])
+    off, sliced = 0, {}
+    for k in keys:
+        sliced[k] = payload[off:off + bufs[k].numel()]
+        off += bufs[k].numel()
+    assert shard.checksum(sliced) == whole
+    bufs["layers.3.q_proj"][17] ^= 1
+    assert shard.checksum(bufs) != whole
