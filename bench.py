@@ -135,13 +135,31 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+CODEC_SOURCES = ("hif4-contest_b200/csrc/codec.cu", "hif4-contest_b200/csrc/common.cuh",
+                 "hif4-contest_b200/csrc/log2_floor_table.h")
+
+
+def codec_source_sha256() -> str:
+    """sha256 over the sources the fused convert kernel is built from."""
+    import hashlib
+    h = hashlib.sha256()
+    for rel in CODEC_SOURCES:
+        with open(os.path.join(ROOT, rel), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def ncu_summary():
-    """The fused kernel's committed ncu figures (per launch, full size)."""
+    """The fused kernel's committed ncu figures (per launch, full size), only
+    when they were captured from the kernel's current sources (the summary
+    records their sha256); otherwise {} -- a profile of an older kernel does
+    not describe this one."""
     try:
         with open(os.path.join(ROOT, "profiles", "convert_c1_16384.json")) as f:
-            return json.load(f)
+            js = json.load(f)
     except (OSError, ValueError):
         return {}
+    return js if js.get("source_sha256") == codec_source_sha256() else {}
 
 
 def ncu_traffic():
@@ -278,6 +296,7 @@ def run_gpu(args, rank, ws, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, k_ms = float(t[0]), float(t[1])
 
+    kernels = codec_kernel_rooflines(args, codes, e4m3, s_dec, meta, hcodes, rt, signs, dev, stream, sp)
     e2e = e2e_api = None
     if not args.no_e2e:
         e2e = e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dist)
@@ -307,11 +326,16 @@ def run_gpu(args, rank, ws, local_rank):
         "roofline": {"bound": "hbm", "kernel": "hif4x convert_kernel (decode+rot64+searched encode)",
                      "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic, "kernel_ms": k_ms,
-                     "alg_bytes_per_launch": elems * ALG_BYTES_PER_ELEM},
+                     "alg_bytes_per_launch": elems * ALG_BYTES_PER_ELEM,
+                     "traffic_source": (f"profiles/convert_c1_16384.json (ncu, captured from sources "
+                                        f"{ncu_summary().get('source_sha256', '')[:12]}, commit "
+                                        f"{ncu_summary().get('source_commit')})") if traffic else
+                                       "no ncu summary of the current kernel sources"},
         "gpu_launches": 2 * K,
         "clocks": clk.summary(w0, w1),
     }
     line["issue_roofline"] = issue_roofline(k_ms, line["clocks"].get("sm_mhz"), elems)
+    line["codec_kernels"] = kernels
     if e2e is not None:
         e2e_ms, launches_e2e, h2d, d2h = e2e
         line["e2e"] = {"value": ws * elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": h2d,
@@ -336,6 +360,52 @@ def run_gpu(args, rank, ws, local_rank):
                                       "choice, GPTQ, refinement, Gram carries; one 1024-token dynamic call per "
                                       "matrix)", **pipeline}
     print(json.dumps(line), flush=True)
+
+
+def codec_kernel_rooflines(args, codes, e4m3, s_dec, meta, hcodes, rt, signs, dev, stream, sp):
+    """HBM roofline of the codec's other kernels on the same 16384^2 tensor,
+    each timed alone with CUDA events on its stream (3 warm-up launches, then
+    10 timed; 0.3-0.8 GB per launch, above the 126 MB L2): the Algorithm-1
+    convert (packed NVFP4 -> rot64 -> Algorithm 1 -> packed HiF4, 1.125 B/elem),
+    the NVFP4 decode (packed in, bf16 out, 2.5625 B/elem) and the HiF4 decode of
+    the round trip (packed in, bf16 out, 2.5625 B/elem).  The searched convert,
+    the step's dominant kernel, is the line's `roofline`."""
+    import torch
+
+    from hif4x import _lib as L
+    elems = ROWS * COLS
+    peak, peak_kind = measured_peak()
+    meta_a = torch.empty_like(meta)
+    codes_a = torch.empty_like(hcodes)
+    d = L.ConvertDesc()
+    d.rows, d.cols, d.src_kind, d.s_dec = ROWS, COLS, L.SRC_NVFP4_PACKED, s_dec
+    d.src, d.src_scale, d.rot_signs, d.encode_mode = codes.data_ptr(), e4m3.data_ptr(), signs.data_ptr(), L.ENC_ALG1
+    d.meta, d.codes = meta_a.data_ptr(), codes_a.data_ptr()
+    dref = L.ctypes.byref(d)
+    launches = {
+        "convert_kernel (Algorithm 1)": (lambda: L.call("hif4x_convert", dref, sp), 1.125),
+        "nvfp4_decode_packed (bf16 out)": (lambda: L.call("hif4x_nvfp4_decode_packed", L.ptr(codes), L.ptr(e4m3),
+                                                          L.f32(s_dec), ROWS, COLS, L.ptr(rt), L.DT_BF16, sp),
+                                           2.5625),
+        "decode_packed_kernel (HiF4 -> bf16)": (lambda: L.call("hif4x_decode_packed", L.ptr(meta), L.ptr(hcodes),
+                                                               ROWS, COLS, L.ptr(rt), L.DT_BF16, sp), 2.5625),
+    }
+    out = {}
+    for name, (fn, bpe) in launches.items():
+        for _ in range(3):
+            fn()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(11)]
+        evs[0].record(stream)
+        for k in range(10):
+            fn()
+            evs[k + 1].record(stream)
+        torch.cuda.synchronize(dev)
+        ms = statistics.mean(evs[k].elapsed_time(evs[k + 1]) for k in range(10))
+        gbs = elems * bpe / (ms * 1e-3) / 1e9
+        out[name] = {"ms": ms, "alg_bytes_per_elem": bpe, "achieved_gbs": gbs, "peak_gbs": peak,
+                     "peak_source": peak_kind, "frac": gbs / peak}
+    del meta_a, codes_a
+    return out
 
 
 def e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dist):
@@ -581,6 +651,71 @@ def e2e_api_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, barrier, dist):
     return ms, launches, h2d, d2h
 
 
+def run_matrix(args, rank, ws, local_rank):
+    """--workload matrix: one Llama-3-8B-shaped matrix (--matrix, e.g.
+    down_proj) calibrated alone on one GPU, the weight-set object's inputs
+    (8192 calibration tokens in 4 samples, one 1024-token dynamic call), with
+    the calibration's phase times from CUDA events (linear.calibrate_weight's
+    info).  A profiling and latency workload: every rank runs its own copy."""
+    import torch
+
+    from hif4x import linear, shard, synth
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    N, C, input_id = shard.LLAMA3_8B_LAYER[args.matrix]
+    T_cal, n_cal, T_test = 8192, 4, 1024
+
+    def pair(x):
+        return list(synth.reference_form(*synth.quantize_nvfp4(x)))
+
+    def acts(seed, T):
+        if input_id == "mlp_act":
+            return synth.acts_silu(seed, T, C, device=dev)
+        return synth.acts_outlier(seed, T, C, n_out=max(1, round(C * 0.002)), gain=20.0, device=dev)
+
+    calib = [pair(acts(10 * i + 1, T_cal // n_cal)) for i in range(n_cal)]
+    test = pair(acts(99, T_test))
+    g = torch.Generator(device=dev).manual_seed(7)
+    wpair = pair((torch.randn(N, C, device=dev, generator=g) * 0.02).to(torch.bfloat16))
+    torch.cuda.synchronize(dev)
+
+    def step(info=None):
+        res = linear.calibrate_weight(wpair[0], wpair[1], calib, info=info, return_device=True,
+                                      rng=torch.Generator().manual_seed(0))
+        linear.dynamic_activation(test[0], test[1], res["activation_state"], return_device=True)
+
+    clk = ClockSampler(physical_gpu(local_rank))
+    clk.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    w0 = time.time()
+    evs[0].record()
+    for k in range(args.steps):
+        step()
+        evs[k + 1].record()
+    torch.cuda.synchronize(dev)
+    w1 = time.time()
+    clk.stop()
+    step_ms = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
+    info = {}
+    step(info)
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": f"one {args.matrix} calibration + one dynamic call, ms", "value": statistics.median(step_ms),
+        "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "step_ms": step_ms, "clocks": clk.summary(w0, w1),
+        "phases_ms": info.get("phases_ms"), "decisions": {k: info.get(k) for k in ("alpha", "mode", "gptq_w",
+                                                                                  "gptq_act", "e3", "tmax")},
+        "config": {"workload": f"{args.matrix} {N}x{C}, {T_cal} calibration tokens ({n_cal} x {T_cal // n_cal}), "
+                               f"1 x {T_test} dynamic tokens", "dtype": "f32", "data": "synthetic"},
+        "timing_note": "CUDA events around each step on the current stream (the calibration's side streams "
+                       "join it); phases from a further, separately timed step",
+    }), flush=True)
+
+
 def run_layer(args, rank, ws, local_rank):
     """--workload layer: the weight-set pipeline alone, with the API legs."""
     res = weightset_bench(rank, ws, local_rank, args.layers, 4096, 4, 1024, args.steps, args.warmup, args.workers,
@@ -700,7 +835,8 @@ def main():
     ap.add_argument("--impl", default="hif4x", choices=["hif4x", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
-    ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention"])
+    ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention", "matrix"])
+    ap.add_argument("--matrix", default="down_proj", help="matrix workload: Llama-3-8B layer matrix name")
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
     ap.add_argument("--workers", type=int, default=3, help="layer workload: matrices in flight per GPU")
     ap.add_argument("--no-pipeline", action="store_true", help="codec workload: skip the weight-set object")
@@ -719,6 +855,8 @@ def main():
     try:
         if args.workload == "layer":
             run_layer(args, rank, ws, local_rank)
+        elif args.workload == "matrix":
+            run_matrix(args, rank, ws, local_rank)
         elif args.workload == "attention":
             run_attention(args, rank, ws, local_rank)
         else:

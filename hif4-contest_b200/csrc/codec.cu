@@ -876,6 +876,60 @@ __global__ void nvfp4_decode_kernel(int src_kind, const void *src, int src_dtype
   }
 }
 
+// Packed NVFP4 -> bf16 / fp32, the layout of decode_packed_kernel: each
+// thread decodes eight 8-element sub-blocks (lane + 32 j of its warp's run of
+// 256), one 4-byte code word each, so a warp's loads and its 16-byte stores are
+// contiguous.  Per sub-block the 8 magnitudes bf16(E2M1[i] * s) of its scale
+// are built once as byte tables and picked per nibble by byte permutes (as
+// load_group does); the nibble's bit 3 becomes the bf16 sign bit, so a
+// negative-zero code decodes to -0 as the reference's -0.0 carrier does.
+__global__ void __launch_bounds__(256) nvfp4_decode_packed_kernel(const uint32_t *__restrict__ codes,
+                                                                  const uint8_t *__restrict__ e4m3, float s_dec,
+                                                                  int64_t nsub, void *out, int out_dtype) {
+  const int lane = threadIdx.x & 31;
+  const int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * (32 * kDecSubs) + lane;
+  uint32_t w[kDecSubs], sc[kDecSubs];
+#pragma unroll
+  for (int j = 0; j < kDecSubs; j++) {
+    const int64_t t = base + 32 * j;
+    w[j] = t < nsub ? __ldcs(codes + t) : 0u;
+    sc[j] = t < nsub ? (uint32_t)__ldg(e4m3 + (t >> 1)) : 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < kDecSubs; j++) {
+    const int64_t t = base + 32 * j;
+    if (t >= nsub) return;
+    const float sk = __fmul_rn(e4m3_to_f32(sc[j]), s_dec);
+    uint32_t W[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(__fmul_rn(kE2M1[2 * i], sk), __fmul_rn(kE2M1[2 * i + 1], sk));
+      W[i] = *reinterpret_cast<const uint32_t *>(&b2);
+    }
+    const uint32_t Hlo = __byte_perm(W[0], W[1], 0x7531), Hhi = __byte_perm(W[2], W[3], 0x7531);
+    const uint32_t Llo = __byte_perm(W[0], W[1], 0x6420), Lhi = __byte_perm(W[2], W[3], 0x6420);
+    uint32_t o[4];   // bf16 pairs of elements (0,1), (2,3), (4,5), (6,7)
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const uint32_t c16 = (w[j] >> (16 * q)) & 0xffffu;
+      const uint32_t sel = c16 & 0x7777u;
+      const uint32_t hi4 = __byte_perm(Hlo, Hhi, sel), lo4 = __byte_perm(Llo, Lhi, sel);
+      // nibble sign bits 3, 7, 11, 15 of c16 -> bits 15 and 31 of the pairs
+      o[2 * q] = __byte_perm(lo4, hi4, 0x5140) | ((c16 & 0x8u) << 12) | ((c16 & 0x80u) << 24);
+      o[2 * q + 1] = __byte_perm(lo4, hi4, 0x7362) | ((c16 & 0x800u) << 4) | ((c16 & 0x8000u) << 16);
+    }
+    if (out_dtype == HIF4X_DT_F32) {
+      float4 *d = reinterpret_cast<float4 *>(out) + t * 2;
+      __stcs(d, make_float4(__uint_as_float(o[0] << 16), __uint_as_float(o[0] & 0xffff0000u),
+                            __uint_as_float(o[1] << 16), __uint_as_float(o[1] & 0xffff0000u)));
+      __stcs(d + 1, make_float4(__uint_as_float(o[2] << 16), __uint_as_float(o[2] & 0xffff0000u),
+                                __uint_as_float(o[3] << 16), __uint_as_float(o[3] & 0xffff0000u)));
+    } else {
+      __stcs(reinterpret_cast<uint4 *>(out) + t, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
 // standalone rotation: one thread per group
 __global__ void __launch_bounds__(kConvThreads) rotate64_kernel(const float *x, const uint64_t *signs, int64_t ngroups,
                                                                  int64_t nb, float *out) {
@@ -954,10 +1008,15 @@ extern "C" int hif4x_nvfp4_decode_packed(const uint8_t *codes, const uint8_t *e4
                                          int64_t cols, void *out, int out_dtype, void *stream) {
   if (!codes || !e4m3 || !out || rows < 0 || cols % 16 != 0 || (reinterpret_cast<uintptr_t>(codes) & 7u))
     return HIF4X_ERR_ARG;
-  const int64_t nblk = rows * (cols / 16);
-  if (nblk == 0) return HIF4X_OK;
-  nvfp4_decode_kernel<<<nblocks(nblk, 256), 256, 0, (cudaStream_t)stream>>>(
-      HIF4X_SRC_NVFP4_PACKED, codes, 0, e4m3, 0, s_dec, nblk, out, out_dtype);
+  const int64_t nsub = rows * (cols / 8);
+  if (nsub == 0) return HIF4X_OK;
+  if (!al16(out)) {   // the vector stores need a 16-byte aligned output; the one-block-per-thread kernel does not
+    nvfp4_decode_kernel<<<nblocks(nsub / 2, 256), 256, 0, (cudaStream_t)stream>>>(
+        HIF4X_SRC_NVFP4_PACKED, codes, 0, e4m3, 0, s_dec, nsub / 2, out, out_dtype);
+  } else {
+    nvfp4_decode_packed_kernel<<<nblocks(nsub, 256 * kDecSubs), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint32_t *>(codes), e4m3, s_dec, nsub, out, out_dtype);
+  }
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
 }

@@ -1178,6 +1178,213 @@ extern "C" int hif4x_gptq(const float *X, const float *unit, const float *U, int
   return HIF4X_OK;
 }
 
+// --------------------------------------------------------------------------
+// The upper factor of the rotated space from the unrotated one.
+//
+// The rotated Hessian is H1 = M^T H0 M, M the block-diagonal orthogonal
+// rotation of _rot_blocks (64 x 64 blocks H64/8 with column signs;
+// solution.py:222-245), and the damping is the same in both spaces (the mean
+// diagonal is the trace over n, which M preserves).  So H1_d^-1 = M^T H0_d^-1 M
+// = (U0 M)^T (U0 M), and U1 = chol_upper(H1_d^-1) is the R factor (positive
+// diagonal) of a QR decomposition of Y = U0 M.  Y is U0 with each row's
+// 64-blocks rotated: upper triangular except for dense 64 x 64 diagonal
+// blocks D_b.  With D_b = Q_b R_b, Q = diag(Q_b) gives Q^T Y upper triangular,
+// so U1 = [R_b on the diagonal, Q_b^T Y[b, c] above it]: 64 independent
+// Householder QRs of 64 x 64 blocks and (n/64)^2/2 products of 64 x 64 blocks
+// (about 64 n^2 multiply-adds) in place of a Gram of the rotated activations
+// and a second Cholesky-inverse (about n^3).
+
+// One CTA per 64 x 64 diagonal block of Y (leading dim n): Householder QR in
+// shared memory (LAPACK's reflector convention), the explicit Q_b written to
+// Qw[b] (row-major 64 x 64), R_b written over the block with zeros below the
+// diagonal; rows of R_b with a negative diagonal are negated together with
+// the matching columns of Q_b, so the factor's diagonal is positive.
+__global__ void __launch_bounds__(256) block_qr64_kernel(float *Y, int64_t n, float *Qw) {
+  // A: the block, then R above the diagonal and reflector k below it in
+  // column k (its leading 1 implicit); Qs: the explicit Q_b
+  __shared__ float A[64][65];
+  __shared__ float Qs[64][65];
+  __shared__ float tau[64], w[64], red[2];
+  const int64_t b = blockIdx.x;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  float *D = Y + (b * 64) * n + b * 64;
+  for (int e = t; e < 4096; e += 256) A[e >> 6][e & 63] = D[(int64_t)(e >> 6) * n + (e & 63)];
+  __syncthreads();
+  for (int k = 0; k < 64; k++) {
+    if (warp == 0) {
+      // sigma = sum_{i > k} A[i][k]^2
+      const int i0 = k + 1 + lane, i1 = k + 33 + lane;
+      const float x0 = i0 < 64 ? A[i0][k] : 0.0f, x1 = i1 < 64 ? A[i1][k] : 0.0f;
+      float sq = x0 * x0 + x1 * x1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      const float alpha = A[k][k];
+      float tk = 0.0f, scale = 0.0f, beta = alpha;
+      if (sq > 0.0f) {
+        beta = -copysignf(sqrtf(alpha * alpha + sq), alpha);
+        tk = (beta - alpha) / beta;
+        scale = 1.0f / (alpha - beta);
+      }
+      __syncwarp();
+      if (i0 < 64) A[i0][k] = x0 * scale;
+      if (i1 < 64) A[i1][k] = x1 * scale;
+      if (lane == 0) {
+        tau[k] = tk;
+        red[0] = beta;
+      }
+    }
+    __syncthreads();
+    // w_j = sum_{i >= k} v_i A[i][j] for j > k: four threads per column
+    {
+      const int j = t >> 2, part = t & 3;
+      float acc = 0.0f;
+      if (j > k)
+        for (int i = k + part; i < 64; i += 4) acc = fmaf(i == k ? 1.0f : A[i][k], A[i][j], acc);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (part == 0) w[j] = acc;
+    }
+    __syncthreads();
+    const float tk = tau[k];
+    for (int e = t; e < 4096; e += 256) {
+      const int i = e >> 6, j = e & 63;
+      if (i >= k && j > k) A[i][j] = fmaf(-tk * (i == k ? 1.0f : A[i][k]), w[j], A[i][j]);
+    }
+    if (t == 0) A[k][k] = red[0];
+    __syncthreads();
+  }
+  // Q = H_0 H_1 ... H_63 I, accumulated backwards: Q <- H_k Q on rows k..63
+  for (int e = t; e < 4096; e += 256) Qs[e >> 6][e & 63] = (e >> 6) == (e & 63) ? 1.0f : 0.0f;
+  __syncthreads();
+  for (int k = 63; k >= 0; k--) {
+    {
+      const int j = t >> 2, part = t & 3;
+      float acc = 0.0f;
+      for (int i = k + part; i < 64; i += 4) acc = fmaf(i == k ? 1.0f : A[i][k], Qs[i][j], acc);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (part == 0) w[j] = acc;
+    }
+    __syncthreads();
+    const float tk = tau[k];
+    for (int e = t; e < 4096; e += 256) {
+      const int i = e >> 6, j = e & 63;
+      if (i >= k) Qs[i][j] = fmaf(-tk * (i == k ? 1.0f : A[i][k]), w[j], Qs[i][j]);
+    }
+    __syncthreads();
+  }
+  // positive diagonal: negate row k of R and column k of Q where R[k][k] < 0
+  float *Q = Qw + b * 4096;
+  for (int e = t; e < 4096; e += 256) {
+    const int i = e >> 6, j = e & 63;
+    const float rs = A[i][i] < 0.0f ? -1.0f : 1.0f;   // row i of R
+    const float qs = A[j][j] < 0.0f ? -1.0f : 1.0f;   // column j of Q
+    D[(int64_t)i * n + j] = j >= i ? rs * A[i][j] : 0.0f;
+    Q[e] = qs * Qs[i][j];
+  }
+}
+
+// Y[b, c] <- Q_b^T Y[b, c] for every 64 x 64 block above the diagonal
+// (c > b), in place: one CTA per block, 4 x 4 outputs per thread.
+__global__ void __launch_bounds__(256) block_qt_apply_kernel(float *Y, int64_t n, const float *Qw) {
+  const int64_t c = blockIdx.x, b = blockIdx.y;
+  if (c <= b) return;
+  __shared__ float Qt[64][65];   // Qt[k][i] = Q_b[i][k]
+  __shared__ float X[64][65];
+  const int t = threadIdx.x;
+  float *blk = Y + (b * 64) * n + c * 64;
+  const float *Q = Qw + b * 4096;
+  for (int e = t; e < 4096; e += 256) {
+    const int i = e >> 6, j = e & 63;
+    Qt[j][i] = Q[e];
+    X[i][j] = blk[(int64_t)i * n + j];
+  }
+  __syncthreads();
+  const int r0 = (t >> 4) * 4, c0 = (t & 15) * 4;
+  float acc[4][4] = {};
+  for (int i = 0; i < 64; i++) {
+    float qv[4], xv[4];
+#pragma unroll
+    for (int a = 0; a < 4; a++) qv[a] = Qt[r0 + a][i];
+#pragma unroll
+    for (int d = 0; d < 4; d++) xv[d] = X[i][c0 + d];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+      for (int d = 0; d < 4; d++) acc[a][d] = fmaf(qv[a], xv[d], acc[a][d]);
+  }
+#pragma unroll
+  for (int a = 0; a < 4; a++)
+    *reinterpret_cast<float4 *>(blk + (int64_t)(r0 + a) * n + c0) = make_float4(acc[a][0], acc[a][1], acc[a][2],
+                                                                                  acc[a][3]);
+}
+
+extern "C" int hif4x_rotate64(const float *x, const uint64_t *signs, int64_t rows, int64_t cols, float *out,
+                              void *stream);
+
+extern "C" int hif4x_chol_rotate64(const float *U0, int64_t n, const uint64_t *signs, float *U1, float *work,
+                                   void *stream) {
+  if (n <= 0 || n % 64 != 0 || !U0 || !signs || !U1 || !work || U0 == U1) return HIF4X_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(U1) & 15u) != 0) return HIF4X_ERR_ARG;
+  const int64_t nb = n / 64;
+  if (nb > 65535) return HIF4X_ERR_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = hif4x_rotate64(U0, signs, n, n, U1, stream);   // Y = U0 M, row by row
+  if (st) return st;
+  block_qr64_kernel<<<(unsigned)nb, 256, 0, s>>>(U1, n, work);
+  block_qt_apply_kernel<<<dim3((unsigned)nb, (unsigned)nb), 256, 0, s>>>(U1, n, work);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+// Copy the lower triangle of the n x n matrix G (leading dim ld) onto its
+// upper triangle, one 32 x 32 tile pair per block through shared memory (both
+// the tile read and the transposed write coalesced); blocks above the
+// diagonal exit at once.
+__global__ void mirror_lower_kernel(float *G, int64_t n, int64_t ld) {
+  __shared__ float tile[32][33];
+  const int64_t bi = blockIdx.y, bj = blockIdx.x;   // source tile (bi, bj), bi >= bj
+  if (bj > bi) return;
+  const int tx = threadIdx.x, ty = threadIdx.y;     // 32 x 8
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int64_t r = bi * 32 + ty + 8 * k, c = bj * 32 + tx;
+    tile[ty + 8 * k][tx] = (r < n && c < n) ? G[r * ld + c] : 0.0f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int64_t r = bj * 32 + ty + 8 * k, c = bi * 32 + tx;   // destination (r, c) = source (c, r)
+    if (r < n && c < n && c > r) G[r * ld + c] = tile[tx][ty + 8 * k];
+  }
+}
+
+// G = X^T X + beta G for X (T x C, leading dim ldx): only the output tiles on
+// or below the diagonal are computed (about half the multiply-adds of the
+// full product), then the lower triangle is mirrored, so G is exactly
+// symmetric.  Large products on the tensor cores, small ones on the SIMT
+// kernels, as hif4x_gemm.
+extern "C" int hif4x_gram(const float *X, int64_t T, int64_t C, int64_t ldx, float beta, float *G, int64_t ldg,
+                          void *stream) {
+  if (T < 0 || C < 0 || ldx < C || ldg < C) return HIF4X_ERR_ARG;
+  if (C == 0) return HIF4X_OK;
+  if (!G || (T > 0 && !X)) return HIF4X_ERR_ARG;   // an empty X may have no storage
+  cudaStream_t s = (cudaStream_t)stream;
+  if (T == 0) {   // an empty sum: G stays (beta = 1) or becomes zero (beta = 0)
+    if (beta == 1.0f) return HIF4X_OK;
+    if (beta != 0.0f) return HIF4X_ERR_UNSUPPORTED;
+    return cudaMemset2DAsync(G, (size_t)ldg * sizeof(float), 0, (size_t)C * sizeof(float), (size_t)C, s) ==
+                   cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
+  }
+  int st = gemm_dispatch(1, 0, C, C, T, 1.0f, X, ldx, 0, X, ldx, 0, beta, G, ldg, 0, 1, 1, s);
+  if (st) return st;
+  const int64_t nt = (C + 31) / 32;
+  if (nt > 65535) return HIF4X_ERR_ARG;
+  mirror_lower_kernel<<<dim3((unsigned)nt, (unsigned)nt), dim3(32, 8), 0, s>>>(G, C, ldg);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
 extern "C" int hif4x_refine_rows(float *M, float *v4, const float *d, const float *G, int64_t T, int64_t C,
                                  int rounds, int *flips, void *stream) {
   if (T < 0 || C <= 0 || rounds < 0) return HIF4X_ERR_ARG;

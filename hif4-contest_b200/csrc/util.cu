@@ -32,6 +32,30 @@ __global__ void col_sum_chunks_kernel(const float *partial, int64_t C, float *ou
   out[c] = accumulate ? out[c] + s : s;
 }
 
+// partial[ch][c] = sum_{r in chunk ch} X[r][c]^2 in float64 (each square is
+// exact in float64; the sums of the few-bit HiF4 values that feed it are exact)
+__global__ void col_sumsq_partial_kernel(const float *X, int64_t R, int64_t C, double *partial) {
+  const int64_t c = (int64_t)blockIdx.x * UT + threadIdx.x;
+  const int ch = blockIdx.y;
+  if (c >= C) return;
+  const int64_t rows_per = (R + kRowChunks - 1) / kRowChunks;
+  const int64_t r0 = ch * rows_per, r1 = min(R, r0 + rows_per);
+  double s = 0.0;
+  for (int64_t r = r0; r < r1; r++) {
+    const double x = (double)X[r * C + c];
+    s = __dadd_rn(s, __dmul_rn(x, x));
+  }
+  partial[(int64_t)ch * C + c] = s;
+}
+
+__global__ void col_sumsq_final_kernel(const double *partial, int64_t C, float *out) {
+  const int64_t c = (int64_t)blockIdx.x * UT + threadIdx.x;
+  if (c >= C) return;
+  double s = 0.0;
+  for (int ch = 0; ch < kRowChunks; ch++) s = __dadd_rn(s, partial[(int64_t)ch * C + c]);
+  out[c] = __double2float_rn(s);
+}
+
 // m = max(abs_sum / n_tok, 1e-12); logm = log(m) - mean(log m)
 // (example/solution/solution.py:855-857); one CTA.
 __global__ void __launch_bounds__(1024) smooth_logm_kernel(const float *abs_sum, int64_t C, float inv_ntok,
@@ -257,6 +281,15 @@ extern "C" int hif4x_col_abs_sum(const float *X, int64_t R, int64_t C, float *ou
   cudaStream_t s = (cudaStream_t)stream;
   col_abs_partial_kernel<<<dim3(nb_(C), kRowChunks), UT, 0, s>>>(X, R, C, work);
   col_sum_chunks_kernel<<<nb_(C), UT, 0, s>>>(work, C, out, accumulate);
+  HIF4X_CHECK_LAUNCH();
+  return HIF4X_OK;
+}
+
+extern "C" int hif4x_col_sumsq(const float *X, int64_t R, int64_t C, float *out, double *work, void *stream) {
+  if (R < 0 || C <= 0 || !out || !work || (R > 0 && !X)) return HIF4X_ERR_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  col_sumsq_partial_kernel<<<dim3(nb_(C), kRowChunks), UT, 0, s>>>(X, R, C, work);
+  col_sumsq_final_kernel<<<nb_(C), UT, 0, s>>>(work, C, out);
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
 }

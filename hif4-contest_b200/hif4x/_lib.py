@@ -63,11 +63,13 @@ SIGNATURES: dict[str, list] = {
     "hif4x_pack_dict5": [vp, vp, vp, vp, vp, i64, i64, vp, vp, vp],
     "hif4x_unpack_dict5": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp],
     "hif4x_gemm": [i32, i32, i64, i64, i64, f32, vp, i64, i64, vp, i64, i64, f32, vp, i64, i64, i64, vp],
+    "hif4x_gram": [vp, i64, i64, i64, f32, vp, i64, vp],
     "hif4x_chol_upper_inv": [vp, i64, i64, f32, vp, vp, vp, vp],
     "hif4x_chol_upper_inv_async": [vp, i64, i64, f32, vp, vp, vp, vp],
     "hif4x_gptq": [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp],
     "hif4x_refine_rows": [vp, vp, vp, vp, i64, i64, i32, vp, vp],
     "hif4x_col_abs_sum": [vp, i64, i64, vp, i32, vp, vp],
+    "hif4x_col_sumsq": [vp, i64, i64, vp, vp, vp],
     "hif4x_smooth_logm": [vp, i64, i64, vp, vp],
     "hif4x_exp_scale": [vp, i64, f32, vp, vp],
     "hif4x_gather_rows": [vp, vp, i64, i64, vp, vp],
@@ -84,6 +86,7 @@ SIGNATURES: dict[str, list] = {
     "hif4x_attention": [vp, vp, vp, i64, i32, i32, i32, vp, vp],
     "hif4x_heads_transpose": [vp, i64, i64, i64, i32, vp, vp],
     "hif4x_chol_upper_inv_noalloc": [vp, i64, i64, f32, vp, vp],
+    "hif4x_chol_rotate64": [vp, i64, vp, vp, vp, vp],
     "hif4x_gemm_tc": [i32, i32, i64, i64, i64, f32, vp, i64, vp, i64, f32, vp, i64, vp],
     "hif4x_device_status": [vp],
     "hif4x_wait_selftest": [ctypes.c_longlong, vp, vp],

@@ -64,8 +64,17 @@ def gemm_batched(A, B, *, ta=False, tb=False, alpha=1.0, beta=0.0, out=None):
 
 
 def gram(X: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
-    """X^T X (C x C), optionally accumulated into out."""
-    return gemm(X, X, ta=True, beta=1.0 if accumulate else 0.0, out=out)
+    """X^T X (C x C), optionally accumulated into out: the lower tiles only,
+    mirrored (hif4x_gram), so the result is exactly symmetric."""
+    T, C = X.shape
+    assert X.stride(1) == 1
+    if out is None:
+        out = torch.empty(C, C, dtype=torch.float32, device=X.device)
+        accumulate = False
+    assert out.stride(1) == 1 and out.shape == (C, C)
+    L.call("hif4x_gram", L.ptr(X), T, C, X.stride(0), L.f32(1.0 if accumulate else 0.0), L.ptr(out), out.stride(0),
+           _s(X))
+    return out
 
 
 def chol_upper_inv(H: torch.Tensor, damp: float = GPTQ_DAMP) -> torch.Tensor | None:
@@ -82,6 +91,18 @@ def chol_upper_inv(H: torch.Tensor, damp: float = GPTQ_DAMP) -> torch.Tensor | N
     if st == L.NOT_PD:
         return None
     return U if batched else U[0]
+
+
+def chol_rotate64(U0: torch.Tensor) -> torch.Tensor:
+    """The upper factor of the rotated space's damped inverse Hessian from the
+    unrotated space's U0 (hif4x_chol_rotate64): a blockwise QR of U0 M, no
+    second Gram or Cholesky."""
+    from .codec import rot_signs
+    n = U0.shape[0]
+    U1 = torch.empty_like(U0)
+    work = torch.empty(64 * n, dtype=torch.float32, device=U0.device)
+    L.call("hif4x_chol_rotate64", L.ptr(U0), n, L.ptr(rot_signs(n // 64, U0.device)), L.ptr(U1), L.ptr(work), _s(U0))
+    return U1
 
 
 class CholLaunch:
@@ -139,6 +160,15 @@ def col_abs_sum(X: torch.Tensor, out: torch.Tensor, accumulate: bool = True) -> 
     R, C = X.shape
     work = torch.empty(64 * C, dtype=torch.float32, device=X.device)
     L.call("hif4x_col_abs_sum", L.ptr(X), R, C, L.ptr(out), int(accumulate), L.ptr(work), _s(out))
+    return out
+
+
+def col_sumsq(X: torch.Tensor) -> torch.Tensor:
+    """Per-column sum of squares (float64 accumulation, one rounding to fp32)."""
+    R, C = X.shape
+    out = torch.empty(C, dtype=torch.float32, device=X.device)
+    work = torch.empty(64 * C, dtype=torch.float64, device=X.device)
+    L.call("hif4x_col_sumsq", L.ptr(X), R, C, L.ptr(out), L.ptr(work), _s(X))
     return out
 
 

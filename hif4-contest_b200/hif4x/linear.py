@@ -105,9 +105,12 @@ def _side_stream(dev) -> torch.cuda.Stream:
 def _act_factor_launch(q: torch.Tensor):
     """Ha = q^T q, act order = argsort(diag Ha) descending, and the damped
     Cholesky-inverse of the permuted Ha launched on the current stream
-    (solution.py:941-951)."""
+    (solution.py:941-951).  The order's key is the diagonal summed exactly
+    (col_sumsq), as the reference's fp32 product gives it for HiF4 values,
+    not the tensor-core Gram's diagonal, whose truncating accumulation moves
+    near-equal columns."""
     Ha = la.gram(q)
-    order = la.argsort_desc(la.diag(Ha))
+    order = la.argsort_desc(la.col_sumsq(q))
     return Ha, order, la.chol_upper_inv_launch(la.permute_sym(Ha, order))
 
 
@@ -229,32 +232,35 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         sub = _randperm(xh_last.shape[0], 128, dev, rng)
         xh_sub = la.gather_rows(xh_last, sub)
         w_sub = la.gather_rows(w_s, rsub)
-        # the two spaces are independent: each runs its Hessian, Cholesky-inverse
-        # and GPTQ proxy on its own stream (the factorisations are latency-bound
-        # for much of their run and overlap well); results are read after both
+        # Only the unrotated space's Hessian is formed and factored: the rotated
+        # space's Hessian is M^T H M for the orthogonal block rotation M, so its
+        # factor follows from U0 by a blockwise QR (la.chol_rotate64), and the
+        # two GPTQ proxies then run on two streams; results are read after both
         main = torch.cuda.current_stream(dev)
         side = _side_stream(dev)
+        Hs = torch.zeros(C, C, dtype=torch.float32, device=dev)
+        for a in acts_s[:-1]:
+            la.gram(a, out=Hs, accumulate=True)
+        chol = la.chol_upper_inv_launch(Hs)
+        del Hs
+        factors = (chol.U, la.chol_rotate64(chol.U))
         side.wait_stream(main)
         runs = []
         for md, stream in ((0, main), (1, side)):
             with torch.cuda.stream(stream):
-                Hs = torch.zeros(C, C, dtype=torch.float32, device=dev)
-                for a in acts_s[:-1]:
-                    la.gram(tf(a, md), out=Hs, accumulate=True)
-                chol = la.chol_upper_inv_launch(Hs)
-                del Hs
                 w_rsub = tf(w_sub, md)
-                qq = la.gptq(w_rsub, _encode_fast(w_rsub)["unit"], chol.U)
+                qq = la.gptq(w_rsub, _encode_fast(w_rsub)["unit"], factors[md])
                 xt = tf(xh_sub, md)
-                runs.append((chol, la.sq_sum_async(_resid(xt, qq, w_rsub)), xt.shape[0] * w_rsub.shape[0]))
+                runs.append((la.sq_sum_async(_resid(xt, qq, w_rsub)), xt.shape[0] * w_rsub.shape[0]))
         main.wait_stream(side)
+        factors[1].record_stream(side)
+        # a non-positive pivot in H0 is one in H1 = M^T H0 M as well (the same
+        # eigenvalues): both spaces take the reference's failed-factor branch
+        ok = chol.finish() is not None
         spaces, cand = [], []
-        for chol, sq, n in runs:
-            U = chol.finish()
-            if U is not None:
-                U.record_stream(main)
-            spaces.append(U)
-            cand.append(float("inf") if U is None else float(sq.item()) / max(n, 1))
+        for U, (sq, n) in zip(factors, runs):
+            spaces.append(U if ok else None)
+            cand.append(float(sq.item()) / max(n, 1) if ok else float("inf"))
         mode = min(range(2), key=lambda i: (cand[i], i)) if not all(math.isnan(c) for c in cand) else 0
         if mode == 1 and spaces[1] is None:
             mode = 0

@@ -184,6 +184,13 @@ int hif4x_gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha
                     int64_t strideA, const float *B, int64_t ldb, int64_t strideB, float beta, float *C,
                     int64_t ldc, int64_t strideC, int64_t batch, void *stream);
 
+/* G = X^T X + beta G (beta 0 or 1), G (C x C, leading dim ldg) exactly
+ * symmetric: the Hessians and Grams of the calibration (example/solution/
+ * solution.py:891-894 sum_i tf_i^T tf_i, 941 and 1011 q^T q, 682-692 Gxx)
+ * with only the tiles on or below the diagonal multiplied, then mirrored.
+ * X: T x C, leading dim ldx. */
+int hif4x_gram(const float *X, int64_t T, int64_t C, int64_t ldx, float beta, float *G, int64_t ldg, void *stream);
+
 /* Tensor-core form of hif4x_gemm (batch 1): tcgen05.mma kind::tf32 with
  * operands split hi + lo (3 products, fp32-faithful), TMA-fed, accumulators
  * in tensor memory.  Needs 16-byte aligned A/B and lda, ldb % 4 == 0, else
@@ -221,6 +228,20 @@ int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, f
 int hif4x_chol_upper_inv_async(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
                                int *info_dev, void *stream);
 
+/* The rotated space's factor from the unrotated one, for the transform
+ * choice (example/solution/solution.py:875-911 factors the Hessian of the
+ * rotated activations anew): with M the block rotation of _rot_blocks
+ * (solution.py:222-245), H1 = M^T H0 M and the damping is the same in both
+ * spaces, so U1 = chol_upper(H1_d^-1) is the positive-diagonal R factor of
+ * U0 M -- upper triangular but for its 64 x 64 diagonal blocks.  Computed as
+ * a Householder QR of each diagonal block and the blocks above it multiplied
+ * by Q_b^T (about 64 n^2 multiply-adds instead of the Gram and Cholesky's n^3).
+ * U0: n x n upper factor of H0_d^-1 (hif4x_chol_upper_inv); signs: the n/64
+ * masks of hif4x_rot_signs (seed0 777); U1: n x n, 16-byte aligned, not U0;
+ * work: 64*n floats.  n % 64 == 0.  Equal to hif4x_chol_upper_inv of the
+ * rotated activations' Gram up to float rounding. */
+int hif4x_chol_rotate64(const float *U0, int64_t n, const uint64_t *signs, float *U1, float *work, void *stream);
+
 /* Allocation-free twin of hif4x_chol_upper_inv (no counterpart in the
  * reference).  For callers that cannot allocate device memory at the call --
  * a host whose device memory another runtime plans up front, or a
@@ -254,6 +275,13 @@ int hif4x_refine_rows(float *M, float *v4, const float *d, const float *G, int64
                       int *flips, void *stream);
 
 /* ---- calibration pipeline: helpers (csrc/util.cu) ---------------------- */
+
+/* Column sums of squares, float64 accumulation rounded once to fp32: the
+ * diagonal of q^T q that orders the act-order permutation (example/solution/
+ * solution.py:946, argsort(Ha.diagonal())).  For the few-bit HiF4 values it
+ * is the exact diagonal, as the reference's fp32 GEMM computes it, where a
+ * tensor-core product's truncating accumulation is not.  work: 64*C doubles. */
+int hif4x_col_sumsq(const float *X, int64_t R, int64_t C, float *out, double *work, void *stream);
 
 /* out[c] (+)= sum_r |X[r][c]| (solution.py:850).  work: 64*C floats. */
 int hif4x_col_abs_sum(const float *X, int64_t R, int64_t C, float *out, int accumulate, float *work,

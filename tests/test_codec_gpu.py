@@ -16,7 +16,7 @@ from conftest import assert_dict5_equal, dict5_from_golden
 pytestmark = pytest.mark.gpu
 
 L = pytest.importorskip("hif4x._lib")
-from hif4x import codec  # noqa: E402
+from hif4x import codec, synth  # noqa: E402
 
 
 def cuda(a):
@@ -34,6 +34,28 @@ def test_decode_packed(codec_golden):
     outb = codec.nvfp4_decode_packed(cuda(g["dec_codes"]), cuda(g["dec_e4m3"]), float(g["dec_sdec"]),
                                      out_dtype=torch.bfloat16)
     np.testing.assert_array_equal(outb.float().cpu().numpy(), g["dec_out"])
+    # negative-zero codes decode to -0 in both output types
+    np.testing.assert_array_equal(np.signbit(out.cpu().numpy()), np.signbit(g["dec_out"]))
+    np.testing.assert_array_equal(np.signbit(outb.float().cpu().numpy()), np.signbit(g["dec_out"]))
+
+
+@pytest.mark.parametrize("rows,cols", [(3, 48), (257, 1040), (64, 4096)])
+def test_decode_packed_ragged_and_unaligned(rows, cols):
+    """The vectorised kernel (16-byte aligned output; tails of a warp's run of
+    sub-blocks) against the one-block-per-thread kernel that an unaligned
+    output takes: identical bits, -0 included."""
+    x = synth.codec_c1(rows + cols, rows, cols)
+    codes, e4m3, s_dec = synth.quantize_nvfp4(x)
+    codes, e4m3 = codes.cuda(), e4m3.cuda()
+    for dt in (torch.float32, torch.bfloat16):
+        aligned = codec.nvfp4_decode_packed(codes, e4m3, s_dec, out_dtype=dt)
+        buf = torch.empty(rows * cols + 8, dtype=dt, device="cuda")
+        off = buf[1:1 + rows * cols]
+        L.call("hif4x_nvfp4_decode_packed", L.ptr(codes), L.ptr(e4m3), L.f32(s_dec), rows, cols, L.ptr(off),
+               L.dtype_code(dt), L.stream())
+        a = aligned.reshape(-1).view(torch.int16 if dt == torch.bfloat16 else torch.int32)
+        b = off.view(torch.int16 if dt == torch.bfloat16 else torch.int32)
+        assert torch.equal(a, b)
 
 
 def test_decode_pairs(codec_golden):

@@ -263,3 +263,66 @@ def test_gptq_production_size_vs_oracle(capsys):
               f"({100 * (og / ow - 1):+.3f} %)")
     assert mism < 0.05
     assert abs(og / ow - 1) < 0.01
+
+
+@pytest.mark.parametrize("T,C", [(50, 70), (700, 1000), (2048, 4160), (1, 33)])
+def test_gram_symmetric_vs_fp64(T, C):
+    """hif4x_gram: the lower tiles (tensor cores from 2^27 multiply-adds on,
+    SIMT below) mirrored onto the upper triangle -- exactly symmetric, within
+    the fp32-GEMM bound of X^T X, and accumulating into a given matrix."""
+    X = rnd(T, C, seed=T + C)
+    G = la.gram(X)
+    assert torch.equal(G, G.T)
+    ref = X.double().T @ X.double()
+    tol = 2e-6 * np.sqrt(T) * float(ref.abs().max()) + 1e-6
+    assert float((G.double() - ref).abs().max()) <= tol
+    base = rnd(C, C, seed=3)
+    base = base + base.T
+    acc = la.gram(X, out=base.clone(), accumulate=True)
+    assert torch.equal(acc, acc.T)
+    assert float((acc.double() - ref - base.double()).abs().max()) <= tol + 1e-5
+
+
+def test_gram_empty_input():
+    G = torch.full((40, 40), 3.0, device="cuda")
+    X = torch.zeros(0, 40, device="cuda")
+    assert torch.equal(la.gram(X, out=G.clone(), accumulate=True), G)
+    assert float(la.gram(X, out=G.clone()).abs().max()) == 0.0
+
+
+def test_col_sumsq_exact_on_hif4_values():
+    """The act-order key: column sums of squares of HiF4 values (few-bit
+    products, exact sums) equal the float64 sums exactly, and a general input
+    is within one fp32 rounding of them."""
+    X = rnd(3000, 704, seed=41, scale=0.05)
+    q = codec.decode(codec.encode(X))
+    got = la.col_sumsq(q).double()
+    ref = (q.double() ** 2).sum(0)
+    assert torch.equal(got, ref.float().double())
+    g2 = la.col_sumsq(X).double()
+    r2 = (X.double() ** 2).sum(0)
+    assert float(((g2 - r2).abs() / r2).max()) <= 2 ** -24
+
+
+@pytest.mark.parametrize("n", [64, 320, 1024, 4096])
+def test_chol_rotate64_matches_the_rotated_factor(n, capsys):
+    """The rotated space's factor derived from the unrotated one (blockwise QR
+    of U0 M) against the direct route of the reference (Gram of the rotated
+    activations, then the damped Cholesky-inverse) and against float64:
+    upper triangular with a positive diagonal, U1^T U1 H1_d = I."""
+    X = rnd(n + 512, n, seed=n + 7)
+    U0 = la.chol_upper_inv(la.gram(X))
+    U1 = la.chol_rotate64(U0)
+    assert torch.equal(U1, torch.triu(U1)) and bool((U1.diagonal() > 0).all())
+    H1 = la.gram(codec.rotate64(X))
+    U1ref = la.chol_upper_inv(H1)
+    rel = float((U1 - U1ref).abs().max() / U1ref.abs().max())
+    Hd = H1.double()
+    Hd.diagonal().add_(float(Hd.diagonal().mean()) * 0.1)
+    Ud = U1.double()
+    R = Ud.T @ (Ud @ Hd)
+    R.diagonal().sub_(1.0)
+    err = float(R.abs().max())
+    with capsys.disabled():
+        print(f"\n  n={n}: |U1 - U1(direct)| = {rel:.1e} of max, |U1^T U1 H1_d - I| = {err:.1e}")
+    assert rel < 2e-4 and err < 1e-3

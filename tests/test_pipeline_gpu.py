@@ -58,11 +58,15 @@ def check_mse(name, got, want, std, report):
 
 def check_order(st, gold_order, Wq, report):
     """Act-order (solution.py:936-951) = argsort of the weight Gram's diagonal,
-    descending.  The diagonal is a fp32 sum whose rounding depends on the
-    summation order and precision (MKL's fp32 there, the tensor cores'
-    3xTF32 here), so columns whose sums differ in the last few bits may swap:
-    at every position where the two orders differ, the two columns' exact
-    (float64) diagonal values must agree to 1e-4 of the largest."""
+    descending.  For HiF4 values that diagonal is an exact sum (the
+    reference's fp32 product and the engine's col_sumsq both give it), so the
+    engine's order must sort its own weights' exact diagonal (to 1e-5 of the
+    largest: the weight refinement may move values after the order is taken),
+    and it may differ from the reference's only where the two sorts break
+    ties differently or the weights themselves differ (the smoothing scale
+    s = exp(alpha log m) is the reference's to an ulp, not bit for bit): at
+    least 95 % of the positions equal, and the diagonal values at the
+    positions agree to 1e-3 of the largest."""
     if st["order"] is None:
         assert gold_order.size == 0
         report.append("act-order: none (as the reference)")
@@ -70,11 +74,23 @@ def check_order(st, gold_order, Wq, report):
     o = st["order"].numpy()
     assert o.shape == gold_order.shape
     d = (Wq.double() ** 2).sum(0).numpy()
+    later_max = np.maximum.accumulate(d[o][::-1])[::-1]
+    unsorted = float((later_max[1:] - d[o][:-1]).max() / d.max()) if o.size > 1 else 0.0
     bad = np.nonzero(o != gold_order)[0]
     dev = float(np.abs(d[o[bad]] - d[gold_order[bad]]).max() / d.max()) if bad.size else 0.0
     report.append(f"act-order: {o.size - bad.size} of {o.size} positions equal; where they differ the "
-                  f"diagonal values agree to {dev:.1e} of the largest")
-    assert dev <= 1e-4, report[-1]
+                  f"diagonal values agree to {dev:.1e} of the largest; own order unsorted by {unsorted:.1e}")
+    assert unsorted <= 1e-5, report[-1]
+    assert bad.size <= 0.05 * o.size and dev <= 1e-3, report[-1]
+
+
+def meta_mismatch(p: dict, meta_ref) -> float:
+    """Fraction of 64-groups whose packed metadata (E6M2 scale, lv2 and lv3
+    bits) differs from the reference's, on the golden file's rows."""
+    npd = {k: v.float().numpy() for k, v in p.items()}
+    rows = pc.code_rows(npd["sign"].shape[0], npd["sign"].shape[1] * 64)
+    meta, _ = oracle.pack_hif4({k: v[rows] for k, v in npd.items()})
+    return float(np.mean(meta != meta_ref))
 
 
 @pytest.mark.parametrize("name", list(pc.LINEAR_CASES) + list(pc.LAYER_CASES))
@@ -91,7 +107,8 @@ def test_linear_case(name, gold, capsys):
     assert st["tmax"] == int(gold[f"{name}/tmax"])
     assert (st["gw"] is not None) == bool(gold[f"{name}/has_gw"])
     np.testing.assert_allclose(st["s"].numpy(), gold[f"{name}/s"], rtol=1e-5)
-    report = [f"weight code mismatch {100 * mismatch(res['weight_params'], gold[name + '/w_meta'], gold[name + '/w_codes']):.2f} %"]
+    report = [f"weight code mismatch {100 * mismatch(res['weight_params'], gold[name + '/w_meta'], gold[name + '/w_codes']):.2f} %, "
+              f"meta mismatch {100 * meta_mismatch(res['weight_params'], gold[name + '/w_meta']):.3f} %"]
     W = pc.deq_nvfp4(wpair).cuda()
     Wq = pc.deq_dict5(res["weight_params"])
     check_order(st, gold[f"{name}/order"], Wq, report)
