@@ -60,7 +60,8 @@ def dist_init():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples at 50 ms while running."""
+    """nvidia-smi clock / throttle samples every `period_ms` while running
+    (200 ms, as the profiling recipe samples; HIF4X_CLOCK_PERIOD_MS overrides)."""
 
     Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -68,6 +69,7 @@ class ClockSampler:
 
     def __init__(self, gpu: int):
         self.gpu = gpu
+        self.period_ms = int(os.environ.get("HIF4X_CLOCK_PERIOD_MS", "200"))
         self.samples = []
         self.proc = None
         self.thread = None
@@ -75,7 +77,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.gpu), "-lms", "50"], stdout=subprocess.PIPE,
+                                          "-i", str(self.gpu), "-lms", str(self.period_ms)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             return
@@ -838,7 +840,7 @@ def main():
     ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention", "matrix"])
     ap.add_argument("--matrix", default="down_proj", help="matrix workload: Llama-3-8B layer matrix name")
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
-    ap.add_argument("--workers", type=int, default=3, help="layer workload: matrices in flight per GPU")
+    ap.add_argument("--workers", type=int, default=6, help="weight sets: matrices in flight per GPU")
     ap.add_argument("--no-pipeline", action="store_true", help="codec workload: skip the weight-set object")
     ap.add_argument("--pipeline-layers", type=int, default=32,
                     help="codec workload: decoder layers of the weight-set object (32 = the full weight set)")
