@@ -5,12 +5,18 @@ Workload (one step): one 16384 x 16384 NVFP4 tensor (N(0, 0.02) bf16,
 E2M1 codes + E4M3 per-16 scales + fp32 tensor scale), converted by the
 fused kernel (decode -> 64-point rotation -> searched HiF4 encode -> packed
 HiF4), then the HiF4 -> bf16 decode round trip.  Inputs and outputs
-(~0.84 GB) exceed the 126 MB L2, so no flush is needed between steps.
+(~0.84 GB) exceed the 126 MB L2, so no flush is needed between steps.  The
+same line carries the host-buffer legs (packed and the reference API's
+pair/dict5 form), the other codec kernels' HBM fractions, and a `pipeline`
+object: the full 32-layer Llama-3-8B-shaped weight set (224 matrices, full
+calibration) converted at N GPUs with its packed result gathered to rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hif4x|reference]
 
 For N > 1 launch with torch.distributed.run; every rank converts its own
-tensor (weak scaling, no data-path collective).  Rank 0 prints one JSON line.
+codec tensor (weak scaling, no data-path collective) and the weight set's
+matrices are split over the ranks (strong scaling).  Rank 0 prints one JSON
+line.
 """
 from __future__ import annotations
 
@@ -655,8 +661,9 @@ def e2e_api_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, barrier, dist):
 
 def run_matrix(args, rank, ws, local_rank):
     """--workload matrix: one Llama-3-8B-shaped matrix (--matrix, e.g.
-    down_proj) calibrated alone on one GPU, the weight-set object's inputs
-    (8192 calibration tokens in 4 samples, one 1024-token dynamic call), with
+    down_proj) calibrated alone on one GPU, with --tokens calibration tokens in
+    4 samples (8192 as the weight-set object, 4096 as the layer workload) and
+    one 1024-token dynamic call, with
     the calibration's phase times from CUDA events (linear.calibrate_weight's
     info).  A profiling and latency workload: every rank runs its own copy."""
     import torch
@@ -665,7 +672,7 @@ def run_matrix(args, rank, ws, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     N, C, input_id = shard.LLAMA3_8B_LAYER[args.matrix]
-    T_cal, n_cal, T_test = 8192, 4, 1024
+    T_cal, n_cal, T_test = args.tokens, 4, 1024
 
     def pair(x):
         return list(synth.reference_form(*synth.quantize_nvfp4(x)))
@@ -685,9 +692,11 @@ def run_matrix(args, rank, ws, local_rank):
         res = linear.calibrate_weight(wpair[0], wpair[1], calib, info=info, return_device=True,
                                       rng=torch.Generator().manual_seed(0))
         linear.dynamic_activation(test[0], test[1], res["activation_state"], return_device=True)
+        return res
 
     clk = ClockSampler(physical_gpu(local_rank))
     clk.start()
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
@@ -698,7 +707,7 @@ def run_matrix(args, rank, ws, local_rank):
         step()
         evs[k + 1].record()
     torch.cuda.synchronize(dev)
-    w1 = time.time()
+    win = (w0, time.time())
     clk.stop()
     step_ms = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
     info = {}
@@ -708,7 +717,7 @@ def run_matrix(args, rank, ws, local_rank):
     print(json.dumps({
         "metric": f"one {args.matrix} calibration + one dynamic call, ms", "value": statistics.median(step_ms),
         "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "step_ms": step_ms, "clocks": clk.summary(w0, w1),
+        "step_ms": step_ms, "clocks": clk.summary(*win),
         "phases_ms": info.get("phases_ms"), "decisions": {k: info.get(k) for k in ("alpha", "mode", "gptq_w",
                                                                                   "gptq_act", "e3", "tmax")},
         "config": {"workload": f"{args.matrix} {N}x{C}, {T_cal} calibration tokens ({n_cal} x {T_cal // n_cal}), "
@@ -839,6 +848,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention", "matrix"])
     ap.add_argument("--matrix", default="down_proj", help="matrix workload: Llama-3-8B layer matrix name")
+    ap.add_argument("--tokens", type=int, default=8192,
+                    help="matrix workload: calibration tokens (4 samples; 8192 as the weight set, 4096 as one layer)")
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
     ap.add_argument("--workers", type=int, default=6, help="weight sets: matrices in flight per GPU")
     ap.add_argument("--no-pipeline", action="store_true", help="codec workload: skip the weight-set object")
