@@ -727,6 +727,65 @@ def run_matrix(args, rank, ws, local_rank):
     }), flush=True)
 
 
+def run_gemm(args, rank, ws, local_rank):
+    """--workload gemm: the tensor-core products of the calibration timed
+    alone with CUDA events and a clock record -- the lower-tile Gram of a
+    Hessian (hif4x_gram: 6144 x 14336, the weight set's down_proj input) and a
+    full NT product (hif4x_gemm, 8192^3) -- against the tensor roofline.  The
+    3xTF32 scheme issues three TF32 MMAs per fp32-equivalent multiply-add;
+    the measured dense bf16 peak (MEASURED_PEAKS.json) bounds TF32 at half of
+    it, so the fp32-equivalent roofline is bf16 / 6."""
+    import torch
+
+    from hif4x import linalg as la
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        bf16, kind = float(pk["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        bf16, kind = 1590.0, "fallback"
+    g = torch.Generator(device=dev).manual_seed(3)
+    X = torch.randn(6144, 14336, device=dev, generator=g)
+    A = torch.randn(8192, 8192, device=dev, generator=g)
+    B = torch.randn(8192, 8192, device=dev, generator=g)
+    G = torch.empty(14336, 14336, device=dev)
+    Cm = torch.empty(8192, 8192, device=dev)
+    cases = {
+        "gram 6144 x 14336 (lower tiles + mirror)": (lambda: la.gram(X, out=G), 6144 * 14336 * 14336.0),
+        "gemm NT 8192^3": (lambda: la.gemm(A, B, tb=True, out=Cm), 2.0 * 8192 ** 3),
+    }
+    clk = ClockSampler(physical_gpu(local_rank))
+    clk.start()
+    time.sleep(0.3)
+    out = {}
+    for name, (fn, flops) in cases.items():
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        w0 = time.time()
+        evs[0].record()
+        for k in range(args.steps):
+            fn()
+            evs[k + 1].record()
+        torch.cuda.synchronize(dev)
+        w1 = time.time()
+        ms = statistics.median(evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps))
+        tfs = flops / (ms * 1e-3) / 1e12
+        out[name] = {"ms": ms, "fp32_equiv_tflops": tfs, "roofline_tflops": bf16 / 6, "frac": tfs / (bf16 / 6),
+                     "clocks": clk.summary(w0, w1)}
+    clk.stop()
+    if rank != 0:
+        return
+    print(json.dumps({"metric": "tensor-core fp32-faithful (3xTF32) products, fp32-equivalent TFLOP/s",
+                      "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "peak_source": f"{kind} bf16 {bf16} TFLOP/s; TF32 = bf16 / 2, 3 TF32 MMAs per product",
+                      "cases": out, "timing_note": "CUDA events per call (split pass included), median"}),
+          flush=True)
+
+
 def run_layer(args, rank, ws, local_rank):
     """--workload layer: the weight-set pipeline alone, with the API legs."""
     res = weightset_bench(rank, ws, local_rank, args.layers, 4096, 4, 1024, args.steps, args.warmup, args.workers,
@@ -846,7 +905,7 @@ def main():
     ap.add_argument("--impl", default="hif4x", choices=["hif4x", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
-    ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention", "matrix"])
+    ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention", "matrix", "gemm"])
     ap.add_argument("--matrix", default="down_proj", help="matrix workload: Llama-3-8B layer matrix name")
     ap.add_argument("--tokens", type=int, default=8192,
                     help="matrix workload: calibration tokens (4 samples; 8192 as the weight set, 4096 as one layer)")
@@ -870,6 +929,8 @@ def main():
             run_layer(args, rank, ws, local_rank)
         elif args.workload == "matrix":
             run_matrix(args, rank, ws, local_rank)
+        elif args.workload == "gemm":
+            run_gemm(args, rank, ws, local_rank)
         elif args.workload == "attention":
             run_attention(args, rank, ws, local_rank)
         else:

@@ -13,7 +13,7 @@
 // made the conversion's loads/stores and the MMA operand reads compete for
 // the shared-memory banks and capped the tensor pipe near 40 %.
 //
-// Persistent kernel, one CTA per SM, 128 x 128 output tiles visited in
+// Persistent kernel, one CTA per SM (all but kTcFreeSms of them), 128 x 128 output tiles visited in
 // bands of GROUP tile-rows (column by column within a band) so that the CTAs
 // running at one time share A and B panels in L2.  192 threads:
 //   warp 0   TMA producer (one lane) + tensor-memory allocation (whole warp)
@@ -43,6 +43,10 @@ constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 2 * BN;            // two accumulator buffers of BN fp32 columns
 constexpr int GROUP = 8;                          // tile-rows per rasterisation band
 constexpr long long SPIN_LIMIT = 1ll << 22;
+// SMs a persistent GEMM leaves free: 16 of 148 took down_proj's calibration
+// (tensor-core Grams and Cholesky products beside one-CTA leaves and GPTQ
+// blocks on side streams) from 106.3 to 104 ms; 8, 24 and 36 did less well
+constexpr int kTcFreeSms = 16;
 
 __device__ int g_status;   // sticky device status: 0 or HIF4X_TIMEOUT
 
@@ -544,7 +548,10 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
-  const int64_t grid = std::min<int64_t>(args.ntiles, sms);
+  // leave kTcFreeSms SMs to the latency-bound kernels of other streams (the
+  // Cholesky leaves and GPTQ column blocks of the same or another
+  // calibration): a persistent grid on every SM holds them off until it ends
+  const int64_t grid = std::min<int64_t>(args.ntiles, sms > 2 * kTcFreeSms ? sms - kTcFreeSms : sms);
   gemm_tc_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, s>>>(ma, mb, args);
   return cudaGetLastError() == cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
 }
