@@ -68,13 +68,22 @@ def _search(x: torch.Tensor):
 
 
 class _Phases:
-    """Optional CUDA-event phase timer (enabled when the caller passes info)."""
+    """Stage markers of a calibration: an NVTX range per stage (always; named
+    hif4x.<stage>, for nsys / `ncu --nvtx --nvtx-include`), and CUDA-event
+    stage times when the caller passes info."""
 
     def __init__(self, on: bool):
         self.on = on
         self.marks = []
+        self.open = False
 
     def mark(self, name: str):
+        if self.open:
+            torch.cuda.nvtx.range_pop()
+            self.open = False
+        if name != "refine_grams":
+            torch.cuda.nvtx.range_push(f"hif4x.{_NEXT_STAGE.get(name, name)}")
+            self.open = True
         if self.on:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
@@ -87,6 +96,11 @@ class _Phases:
         return {self.marks[i + 1][0]: self.marks[i][1].elapsed_time(self.marks[i + 1][1])
                 for i in range(len(self.marks) - 1)}
 
+
+# the stage that starts at each mark (the marks end the stage they are named after)
+_NEXT_STAGE = {"start": "upload_decode", "upload_decode": "alpha_search", "alpha_search": "transform_choice",
+               "transform_choice": "weight_encode_gptq", "weight_encode_gptq": "act_gptq",
+               "act_gptq": "refine_grams"}
 
 _SIDE: dict = {}
 

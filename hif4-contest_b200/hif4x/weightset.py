@@ -95,3 +95,48 @@ def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None
         raise errors[0]
     # results produced on the workers' streams are complete (each synchronised)
     return out
+
+
+def convert_to_dir(jobs: list, out_dir: str, workers: int = 2, device=None, urgent=None) -> dict:
+    """convert() with every finished matrix written to out_dir as soon as it
+    finishes, so a long conversion (a whole weight set runs for seconds on one
+    GPU, the reference's CPU path for hours) that stops part-way resumes where
+    it stopped: matrices whose file is already there are not converted again.
+
+    Each file, out_dir/<key>.pt, holds the packed HiF4 weight (uint8: meta
+    words then codes, shard.pack_params), its shape and the activation state
+    (CPU tensors, as the six-function API returns it), written to a temporary
+    name and renamed, so a file that exists is complete.  Returns
+    {key: path} for every job."""
+    import os
+
+    from . import shard
+
+    os.makedirs(out_dir, exist_ok=True)
+
+    def path(key: str) -> str:
+        return os.path.join(out_dir, key.replace(os.sep, "_") + ".pt")
+
+    def to_cpu(v):
+        if isinstance(v, torch.Tensor):
+            return v.detach().cpu()
+        if isinstance(v, dict):
+            return {k: to_cpu(x) for k, x in v.items()}
+        if isinstance(v, (list, tuple)):
+            return type(v)(to_cpu(x) for x in v)
+        return v
+
+    def consume(key, res, dyn):
+        sf = res["weight_params"]["scale_factor"]
+        rec = {"key": key, "rows": int(sf.shape[0]), "cols": int(sf.shape[1]) * 64,
+               "packed": shard.pack_params(res["weight_params"]).cpu(),
+               "activation_state": to_cpu(res["activation_state"])}
+        tmp = path(key) + ".tmp"
+        torch.save(rec, tmp)
+        os.replace(tmp, path(key))
+        return path(key)
+
+    todo = [j for j in jobs if not os.path.exists(path(j[0]))]
+    if todo:
+        convert(todo, workers=workers, device=device, consume=consume, urgent=urgent)
+    return {j[0]: path(j[0]) for j in jobs}

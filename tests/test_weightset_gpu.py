@@ -91,3 +91,28 @@ def test_urgent_streams_same_results():
             assert torch.equal(getattr(d0, k), getattr(d1, k)), (key, k)
     assert weightset._worker_stream(torch.device("cuda", 0), 0, True).priority < \
         weightset._worker_stream(torch.device("cuda", 0), 0, False).priority
+
+
+def test_convert_to_dir_resumes(tmp_path, monkeypatch):
+    """A conversion stopped part-way resumes: matrices already written are
+    not converted again, the rest are, and every file holds the same packed
+    weights as a direct conversion."""
+    names = ["lin_c1024", "lin_c2560"]
+    jobs = []
+    for name in names:
+        wpair, calib, tests, _ = pc.linear_inputs(name)
+        jobs.append((name, _dev(wpair), [_dev(c) for c in calib], None))
+    paths = weightset.convert_to_dir(jobs[:1], str(tmp_path))      # "stopped" after the first
+    assert list(paths) == ["lin_c1024"]
+    calls = []
+    real = linear.calibrate_weight
+    monkeypatch.setattr(linear, "calibrate_weight", lambda *a, **k: calls.append(1) or real(*a, **k))
+    paths = weightset.convert_to_dir(jobs, str(tmp_path))
+    assert len(calls) == 1 and sorted(paths) == sorted(names)
+    from hif4x import shard
+    for key, wpair, calib, _ in jobs:
+        rec = torch.load(paths[key], weights_only=True)
+        ref = real(wpair[0], wpair[1], calib, return_device=True)
+        assert torch.equal(rec["packed"], shard.pack_params(ref["weight_params"]).cpu()), key
+        assert rec["activation_state"]["mode"] == ref["activation_state"]["mode"]
+        assert (rec["rows"], rec["cols"]) == tuple(wpair[0].shape)
