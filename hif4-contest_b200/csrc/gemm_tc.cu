@@ -160,6 +160,7 @@ struct TcArgs {
   int b_div;                  // product b reads B's product b / b_div
   int64_t c_bstride;          // C elements between products
   int kmode;                  // triangular operand: K-steps a tile may skip (tile_krange)
+  const unsigned *lo_nz;      // bit 0 / 1: A's / B's lo half has a nonzero (null: assume both)
 };
 
 // K-steps [kb, ke) that can be nonzero for output tile (ti, tj) when one
@@ -232,6 +233,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (int)((args.K + BK - 1) / BK);
+  // An operand whose every value is exact in TF32 (HiF4 values, bf16 inputs)
+  // has an all-zero lo half: its lo tiles are neither loaded nor multiplied,
+  // which leaves the sum unchanged (those products are exact zeros).  The
+  // split pass recorded which halves are nonzero; producer and MMA warp read
+  // the same word, so they agree on the stage layout.
+  const unsigned lz = args.lo_nz != nullptr ? *args.lo_nz : 3u;
+  const bool a_lo_on = (lz & 1u) != 0u, b_lo_on = (lz & 2u) != 0u;
+  const uint32_t stage_tx = (uint32_t)TILE_BYTES * (2u + (a_lo_on ? 1u : 0u) + (b_lo_on ? 1u : 0u));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -273,11 +282,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           if (g >= STAGES) ok = mbar_wait(&empty[s], (uint32_t)(((g / STAGES) - 1) & 1));
           if (!ok) break;
           uint8_t *st = smem + s * STAGE_BYTES;
-          mbar_expect_tx(&full[s], STAGE_BYTES);
+          mbar_expect_tx(&full[s], stage_tx);
           tma_load_2d(&mapA, st, &full[s], kt * BK, m0);
-          tma_load_2d(&mapA, st + TILE_BYTES, &full[s], kt * BK, args.a_lo + m0);
+          if (a_lo_on) tma_load_2d(&mapA, st + TILE_BYTES, &full[s], kt * BK, args.a_lo + m0);
           tma_load_2d(&mapB, st + 2 * TILE_BYTES, &full[s], kt * BK, n0);
-          tma_load_2d(&mapB, st + 3 * TILE_BYTES, &full[s], kt * BK, args.b_lo + n0);
+          if (b_lo_on) tma_load_2d(&mapB, st + 3 * TILE_BYTES, &full[s], kt * BK, args.b_lo + n0);
         }
       }
       // drain: every issued copy has landed before the CTA may exit (the
@@ -318,8 +327,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             const uint64_t dah = kmajor_desc(a_hi, j), dal = kmajor_desc(a_lo, j);
             const uint64_t dbh = kmajor_desc(b_hi, j), dbl = kmajor_desc(b_lo, j);
             mma_tf32(d, dah, dbh, idesc, (kt > kb || j > 0) ? 1u : 0u);
-            mma_tf32(d, dah, dbl, idesc, 1u);
-            mma_tf32(d, dal, dbh, idesc, 1u);
+            if (b_lo_on) mma_tf32(d, dah, dbl, idesc, 1u);
+            if (a_lo_on) mma_tf32(d, dal, dbh, idesc, 1u);
           }
           mma_commit(&empty[s]);   // stage s free once these MMAs have read it
         }
@@ -419,7 +428,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 // loads and the stores are coalesced.  blockIdx.z indexes a batch of
 // operands src_bstride apart, written 2 R kp apart.
 __global__ void split_tf32_kernel(const float *__restrict__ src, int64_t ld, int k_contig, int64_t R, int64_t K,
-                                  int64_t src_bstride, float *__restrict__ dst, int64_t kp) {
+                                  int64_t src_bstride, float *__restrict__ dst, int64_t kp, unsigned *lo_nz,
+                                  unsigned lo_bit) {
   __shared__ float tile[32][33];
   src += (int64_t)blockIdx.z * src_bstride;
   dst += (int64_t)blockIdx.z * 2 * R * kp;
@@ -433,16 +443,21 @@ __global__ void split_tf32_kernel(const float *__restrict__ src, int64_t ld, int
     }
     __syncthreads();
   }
+  bool lo_any = false;
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const int64_t r = r0 + ty + 8 * i, k = k0 + tx;
     if (r < R && k < K) {
       const float x = k_contig ? src[r * ld + k] : tile[tx][ty + 8 * i];
       const float hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+      const float lo = __fsub_rn(x, hi);
       dst[r * kp + k] = hi;
-      dst[(R + r) * kp + k] = __fsub_rn(x, hi);
+      dst[(R + r) * kp + k] = lo;
+      lo_any |= lo != 0.0f;
     }
   }
+  // record (once per block) that this operand's lo half is not all zero
+  if (lo_nz != nullptr && __syncthreads_or(lo_any) && tx == 0 && ty == 0) atomicOr(lo_nz, lo_bit);
 }
 
 // ------------------------------------------------------------------ host
@@ -501,17 +516,17 @@ static int device_sms(int dev) {
 }
 
 int split_operand(const float *src, int64_t ld, int k_contig, int64_t R, int64_t K, int64_t src_bstride,
-                  int batch, float *dst, int64_t kp, cudaStream_t s) {
+                  int batch, float *dst, int64_t kp, cudaStream_t s, unsigned *lo_nz, unsigned lo_bit) {
   const int64_t gy = (R + 31) / 32;
   if (gy > 65535 || batch < 1 || batch > 65535) return HIF4X_ERR_UNSUPPORTED;
   dim3 grid((unsigned)((K + 31) / 32), (unsigned)gy, (unsigned)batch);
-  split_tf32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, k_contig, R, K, src_bstride, dst, kp);
+  split_tf32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, k_contig, R, K, src_bstride, dst, kp, lo_nz, lo_bit);
   return HIF4X_OK;
 }
 
 int gemm_split(const float *As, int a_products, const float *Bs, int b_products, int64_t M, int64_t N, int64_t K,
                int64_t kp, float alpha, float beta, float *C, int64_t ldc, int64_t c_bstride, int batch, int b_div,
-               int lower, int kmode, cudaStream_t s) {
+               int lower, int kmode, cudaStream_t s, const unsigned *lo_nz) {
   if (M <= 0 || N <= 0 || K <= 0 || batch < 1 || b_div < 1 || (batch - 1) / b_div >= b_products ||
       batch > a_products)
     return HIF4X_ERR_ARG;
@@ -544,6 +559,7 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
   args.b_div = b_div;
   args.c_bstride = c_bstride;
   args.kmode = (kmode >= 0 && kmode <= 3) ? kmode : 0;
+  args.lo_nz = lo_nz;
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
@@ -589,13 +605,20 @@ int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alph
   const bool same = A == B && lda == ldb && a_kc == b_kc && M == N;
   const int64_t a_floats = 2 * kp * M, b_floats = same ? 0 : 2 * kp * N;
   float *ws = nullptr;
-  if (cudaMallocAsync(reinterpret_cast<void **>(&ws), (size_t)(a_floats + b_floats) * sizeof(float), s) !=
+  // split operands, then one word: which operands have a nonzero lo half
+  if (cudaMallocAsync(reinterpret_cast<void **>(&ws), (size_t)(a_floats + b_floats + 4) * sizeof(float), s) !=
       cudaSuccess)
     return HIF4X_ERR_LAUNCH;
   float *As = ws, *Bs = same ? ws : ws + a_floats;
-  int st = tc::split_operand(A, lda, a_kc, M, K, 0, 1, As, kp, s);
-  if (st == HIF4X_OK && !same) st = tc::split_operand(B, ldb, b_kc, N, K, 0, 1, Bs, kp, s);
-  if (st == HIF4X_OK) st = tc::gemm_split(As, 1, Bs, 1, M, N, K, kp, alpha, beta, C, ldc, 0, 1, 1, lower, kmode, s);
+  unsigned *lo_nz = reinterpret_cast<unsigned *>(ws + a_floats + b_floats);
+  if (cudaMemsetAsync(lo_nz, 0, sizeof(unsigned), s) != cudaSuccess) {
+    cudaFreeAsync(ws, s);
+    return HIF4X_ERR_LAUNCH;
+  }
+  int st = tc::split_operand(A, lda, a_kc, M, K, 0, 1, As, kp, s, lo_nz, same ? 3u : 1u);
+  if (st == HIF4X_OK && !same) st = tc::split_operand(B, ldb, b_kc, N, K, 0, 1, Bs, kp, s, lo_nz, 2u);
+  if (st == HIF4X_OK)
+    st = tc::gemm_split(As, 1, Bs, 1, M, N, K, kp, alpha, beta, C, ldc, 0, 1, 1, lower, kmode, s, lo_nz);
   cudaFreeAsync(ws, s);
   return st;
 }

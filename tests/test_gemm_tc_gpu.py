@@ -102,3 +102,23 @@ def test_bounded_wait_runs_out_and_reports_timeout():
     assert L.lib().hif4x_device_status(L.stream()) == L.OK
     ref = A.double() @ B.double().T
     assert float((got.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * 256 ** 0.5 + 1e-6
+
+
+@pytest.mark.parametrize("exact", ["both", "a", "b"])
+def test_tc_gemm_tf32_exact_operands(exact):
+    """Operands whose values are exact in TF32 (bf16 values here, as the
+    NVFP4-decoded activations and HiF4 values are) leave their lo halves all
+    zero: the kernel then loads and multiplies only the nonzero halves (one
+    or two products instead of three), and the result still meets the
+    fp32-GEMM bound against float64."""
+    M, N, K = 640, 512, 2048
+    A, B = rnd(M, K, seed=21), rnd(N, K, seed=22)
+    if exact in ("both", "a"):
+        A = A.bfloat16().float()
+    if exact in ("both", "b"):
+        B = B.bfloat16().float()
+    ref = A.double() @ B.double().T
+    got = tc_gemm(A, B, 0, 1)
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    err = float((got.double() - ref).abs().max() / ref.abs().max())
+    assert err < 2e-6 * K ** 0.5 + 1e-6, err

@@ -326,3 +326,15 @@ def test_chol_rotate64_matches_the_rotated_factor(n, capsys):
     with capsys.disabled():
         print(f"\n  n={n}: |U1 - U1(direct)| = {rel:.1e} of max, |U1^T U1 H1_d - I| = {err:.1e}")
     assert rel < 2e-4 and err < 1e-3
+
+
+def test_gram_of_hif4_values_exact_products():
+    """q^T q of HiF4 values (the act-order Hessian, gw): one TF32 product per
+    multiply-add, every product exact, the sum within the fp32 bound."""
+    X = rnd(4096, 1024, seed=51, scale=0.05)
+    q = codec.decode(codec.encode(X))
+    G = la.gram(q)
+    ref = q.double().T @ q.double()
+    assert torch.equal(G, G.T)
+    tol = 2e-6 * np.sqrt(4096) * float(ref.abs().max()) + 1e-6
+    assert float((G.double() - ref).abs().max()) <= tol
