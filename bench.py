@@ -752,14 +752,19 @@ def run_gemm(args, rank, ws, local_rank):
     B = torch.randn(8192, 8192, device=dev, generator=g)
     G = torch.empty(14336, 14336, device=dev)
     Cm = torch.empty(8192, 8192, device=dev)
+    H1 = la.gram(X[:, :4096].contiguous())
     cases = {
         "gram 6144 x 14336 (lower tiles + mirror)": (lambda: la.gram(X, out=G), 6144 * 14336 * 14336.0),
         "gemm NT 8192^3": (lambda: la.gemm(A, B, tb=True, out=Cm), 2.0 * 8192 ** 3),
+        # the Cholesky-inverse: n^3/3 multiply-adds for the factor and n^3/3 for the inverse
+        "chol_upper_inv n = 14336": (lambda: la.chol_upper_inv(G), 2.0 * 14336 ** 3 / 3),
+        "chol_upper_inv n = 4096": (lambda: la.chol_upper_inv(H1), 2.0 * 4096 ** 3 / 3),
     }
     clk = ClockSampler(physical_gpu(local_rank))
     clk.start()
     time.sleep(0.3)
     out = {}
+    la.gram(X, out=G)   # a Hessian for the Cholesky cases
     for name, (fn, flops) in cases.items():
         for _ in range(max(3, args.warmup)):
             fn()

@@ -9,6 +9,9 @@
 // rounding.
 #include <algorithm>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 
@@ -1049,27 +1052,75 @@ static int trtri_lower(float *A, int64_t n, int64_t ld, float *work, cudaStream_
 // triangular inverse, and all flops but the 128-row leaves (factor and
 // inverse fused in shared memory by one CTA) run as GEMMs.  A keeps Schur
 // complements, not the factor.  Inv must be zero above the diagonal on entry.
-// Split n1 = n/2 rounded down to a multiple of 128 (at least 128); work holds
-// T (n2 x n1 <= n*n/4 floats), used only after both recursive calls return.
+// Split n1 = n/2 rounded down to a multiple of 128 (at least 128).
+//
+// T = L21 L11^-1 depends only on L21 and L11^-1, not on A22's factorisation,
+// so it runs on a second stream (`side`) from the moment L21 exists, beside
+// the A22 update and recursion, whose leaves and small products leave most
+// SMs idle; the caller's stream waits for it before the last product.  Each
+// recursion depth has its own T buffer (work: n2 x n1 here, the deeper
+// depths after it; about n*n/3 floats in all), because a T of this depth is
+// still needed while the deeper calls compute theirs.
+struct CholSide {
+  cudaStream_t s = nullptr;
+  cudaEvent_t l21 = nullptr;          // L21 written (recorded on the caller's stream)
+  cudaEvent_t t[32] = {};             // T of depth d written (recorded on s)
+};
+
+static CholSide *chol_side(cudaStream_t main) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, CholSide *> sides;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = sides.find({dev, main});
+  if (it != sides.end()) return it->second;
+  CholSide *c = new CholSide();
+  int prio = 0;
+  bool ok = cudaStreamGetPriority(main, &prio) == cudaSuccess &&
+            cudaStreamCreateWithPriority(&c->s, cudaStreamNonBlocking, prio) == cudaSuccess &&
+            cudaEventCreateWithFlags(&c->l21, cudaEventDisableTiming) == cudaSuccess;
+  for (int d = 0; ok && d < 32; d++) ok = cudaEventCreateWithFlags(&c->t[d], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    return nullptr;   // the recursion then runs every product on the caller's stream
+  }
+  sides[{dev, main}] = c;
+  return c;
+}
+
 static int potrf_inv_rec(float *A, int64_t n, int64_t ld, float *Inv, int64_t ldi, int *info_dev, float *work,
-                         cudaStream_t s) {
+                         cudaStream_t s, CholSide *side, int depth) {
   if (n <= PB) return potrf_inv128(A, ld, (int)n, Inv, ldi, info_dev, 3, s);
   const int64_t n1 = std::max<int64_t>(PB, (n / 2 / PB) * PB), n2 = n - n1;
   float *A21 = A + n1 * ld, *A22 = A + n1 * ld + n1;
   float *I11 = Inv, *I21 = Inv + n1 * ldi, *I22 = Inv + n1 * ldi + n1;
-  int st = potrf_inv_rec(A, n1, ld, I11, ldi, info_dev, work, s);
+  float *T = work, *deeper = work + n2 * n1;
+  int st = potrf_inv_rec(A, n1, ld, I11, ldi, info_dev, deeper, s, side, depth + 1);
   if (st) return st;
   // L11^-1 and L22^-1 are lower triangular (zeros above the diagonal in
   // memory): kmode lets the tensor-core products skip their zero K-steps
   st = gemm_dispatch(0, 1, n2, n1, n1, 1.0f, A21, ld, 0, I11, ldi, 0, 0.0f, I21, ldi, 0, 1, 0, s, 1);
   if (st) return st;
+  const bool overlap = side != nullptr && depth < 32;
+  if (overlap) {
+    if (cudaEventRecord(side->l21, s) != cudaSuccess || cudaStreamWaitEvent(side->s, side->l21, 0) != cudaSuccess)
+      return HIF4X_ERR_LAUNCH;
+    st = gemm_dispatch(0, 0, n2, n1, n1, 1.0f, I21, ldi, 0, I11, ldi, 0, 0.0f, T, n1, 0, 1, 0, side->s, 2);
+    if (st) return st;
+    if (cudaEventRecord(side->t[depth], side->s) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+  }
   st = gemm_dispatch(0, 1, n2, n2, n1, -1.0f, I21, ldi, 0, I21, ldi, 0, 1.0f, A22, ld, 0, 1, 1, s);
   if (st) return st;
-  st = potrf_inv_rec(A22, n2, ld, I22, ldi, info_dev, work, s);
+  st = potrf_inv_rec(A22, n2, ld, I22, ldi, info_dev, deeper, s, side, depth + 1);
   if (st) return st;
-  st = gemm_dispatch(0, 0, n2, n1, n1, 1.0f, I21, ldi, 0, I11, ldi, 0, 0.0f, work, n1, 0, 1, 0, s, 2);
-  if (st) return st;
-  return gemm_dispatch(0, 0, n2, n1, n2, -1.0f, I22, ldi, 0, work, n1, 0, 0.0f, I21, ldi, 0, 1, 0, s, 3);
+  if (overlap) {
+    if (cudaStreamWaitEvent(s, side->t[depth], 0) != cudaSuccess) return HIF4X_ERR_LAUNCH;
+  } else {
+    st = gemm_dispatch(0, 0, n2, n1, n1, 1.0f, I21, ldi, 0, I11, ldi, 0, 0.0f, T, n1, 0, 1, 0, s, 2);
+    if (st) return st;
+  }
+  return gemm_dispatch(0, 0, n2, n1, n2, -1.0f, I22, ldi, 0, T, n1, 0, 0.0f, I21, ldi, 0, 1, 0, s, 3);
 }
 
 // In-place inverse of a lower-triangular n x n block at A (leading dim ld):
@@ -1097,14 +1148,16 @@ extern "C" int hif4x_chol_upper_inv_async(const float *H, int64_t n, int64_t bat
   const int64_t nn = n * n;
   if (cudaMemsetAsync(info_dev, 0, sizeof(int), s) != cudaSuccess) return HIF4X_ERR_LAUNCH;
   // work: [nn] reversed damped matrix (overwritten by Schur complements) +
-  // [nn/4] GEMM scratch; L^-1 is built in U itself and reversed in place.
+  // the recursion's T buffers (<= nn/3 + n*128); L^-1 is built in U itself and
+  // reversed in place.
+  CholSide *side = n > PB ? chol_side(s) : nullptr;
   for (int64_t b = 0; b < batch; b++) {
     float *P = work;
     float *Inv = U + b * nn;
     reverse_square_kernel<<<nblk(nn, 256), 256, 0, s>>>(H + b * nn, P, n, nn);
     damp_diag_kernel<<<1, 1024, 0, s>>>(P, n, damp);
     if (cudaMemsetAsync(Inv, 0, (size_t)nn * sizeof(float), s) != cudaSuccess) return HIF4X_ERR_LAUNCH;
-    const int st = potrf_inv_rec(P, n, n, Inv, n, info_dev, work + nn, s);
+    const int st = potrf_inv_rec(P, n, n, Inv, n, info_dev, work + nn, s, side, 0);
     if (st) return st;
     reverse_flat_kernel<<<nblk((nn + 1) / 2, 256), 256, 0, s>>>(Inv, nn);
   }

@@ -216,8 +216,9 @@ int hif4x_wait_selftest(long long spins, int *done_dev, void *stream);
  * matrices.  Computed as U = J L^-1 J with J H J = L L^T: one recursive
  * Cholesky of the index-reversed matrix that builds L^-1 as it goes.
  * Synchronises the stream; returns HIF4X_NOT_PD (U undefined) where the
- * reference's torch Cholesky would raise.  work: 2*n*n floats (1.25*n*n
- * used); info_dev: one device int. */
+ * reference's torch Cholesky would raise.  work: 2*n*n floats (about
+ * 1.34*n*n used); info_dev: one device int.  Part of the products run on a
+ * second stream the library keeps per caller stream, joined before return. */
 int hif4x_chol_upper_inv(const float *H, int64_t n, int64_t batch, float damp, float *U, float *work,
                          int *info_dev, void *stream);
 
