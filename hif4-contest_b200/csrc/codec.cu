@@ -739,24 +739,26 @@ __global__ void __launch_bounds__(256) decode_packed_kernel(const uint32_t *__re
     const int i = (int)(t & 7);
     const int E = (int)((m[j] & 0xffu) >> 2) - 48;
     const float sf = __fmul_rn(exp2i(E), 1.0f + 0.25f * (float)(m[j] & 3u));
-    const uint32_t l2 = (m[j] >> (8 + i)) & 1u;
+    const int l2 = (int)((m[j] >> (8 + i)) & 1u);
+    // sf * lv2 * lv3 / 4 for the two quads of the sub-block (exact powers of two of sf)
+    const float sq0 = __fmul_rn(sf, exp2i(l2 + (int)((m[j] >> (16 + 2 * i)) & 1u) - 2));
+    const float sq1 = __fmul_rn(sf, exp2i(l2 + (int)((m[j] >> (17 + 2 * i)) & 1u) - 2));
     float v[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      const uint32_t l3 = (m[j] >> (16 + 2 * i + k / 4)) & 1u;
       const uint32_t nib = (w[j] >> (4 * k)) & 15u;
-      const float scale = __fmul_rn(sf, exp2i((int)(l2 + l3) - 2));  // sf * lv2 * lv3 / 4, exact
-      const float mag = __fmul_rn((float)(nib & 7u), scale);
-      v[k] = (nib & 8u) ? -mag : mag;
+      const float mag = __fmul_rn((float)(nib & 7u), k < 4 ? sq0 : sq1);
+      v[k] = __uint_as_float(__float_as_uint(mag) | ((nib & 8u) << 28));   // -0 for a negative-zero code
     }
     if (out_dtype == HIF4X_DT_F32) {
       float4 *o = reinterpret_cast<float4 *>(out) + t * 2;
       __stcs(o, make_float4(v[0], v[1], v[2], v[3]));
       __stcs(o + 1, make_float4(v[4], v[5], v[6], v[7]));
     } else {
+      // every HiF4 value is exact in bf16: its pattern is the float's upper half
       uint32_t q[4];
 #pragma unroll
-      for (int n = 0; n < 4; n++) q[n] = (__float_as_uint(v[2 * n]) >> 16) | (__float_as_uint(v[2 * n + 1]) & 0xffff0000u);
+      for (int n = 0; n < 4; n++) q[n] = __byte_perm(__float_as_uint(v[2 * n]), __float_as_uint(v[2 * n + 1]), 0x7632);
       __stcs(reinterpret_cast<uint4 *>(out) + t, make_uint4(q[0], q[1], q[2], q[3]));
     }
   }
