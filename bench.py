@@ -920,7 +920,9 @@ def main():
     ap.add_argument("--pipeline-layers", type=int, default=32,
                     help="codec workload: decoder layers of the weight-set object (32 = the full weight set)")
     ap.add_argument("--pipeline-steps", type=int, default=2, help="timed conversions of the weight set")
-    ap.add_argument("--pipeline-warmup", type=int, default=1, help="untimed conversions of the weight set first")
+    ap.add_argument("--pipeline-warmup", type=int, default=2,
+                    help="untimed conversions of the weight set first (the first ones after start-up still "
+                         "grow the allocator's pools)")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "codec":
         args.warmup = 3
