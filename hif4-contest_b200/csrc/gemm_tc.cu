@@ -21,6 +21,14 @@
 //   warps 2-5 epilogue: tcgen05.ld of their TMEM lane quarter -> alpha/beta
 //            -> global, on one of two accumulator buffers while the MMA
 //            warp fills the other
+// The epilogue writes C through the TMA when beta is 0 or 1 and C allows a
+// tensor map: each warp stages 32 x 32 boxes of its rows in shared memory
+// (128-byte swizzle, so the row-per-lane writes are conflict-free) and one
+// lane issues a bulk tensor store (beta 0) or a bulk tensor add-reduction
+// into C (beta 1: C + v rounded to nearest, the value fmaf(1, C, v) gives).
+// Lane-per-row stores straight from registers touch 32 rows per instruction
+// and made products with short K (the rank-128 updates of GPTQ) bound by
+// the epilogue; other betas and batched products keep that path.
 // Every mbarrier wait is bounded: on expiry the kernel records
 // HIF4X_TIMEOUT in a device status word and finishes without further
 // waits; hif4x_device_status() reports it.
@@ -38,7 +46,10 @@ namespace tc {
 constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
 constexpr int TILE_BYTES = BM * BK * 4;           // 16 KiB (A and B tiles are the same size)
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;        // A hi, A lo, B hi, B lo
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* align */ + 256 /* barriers */;
+// epilogue staging: per epilogue warp two 32 x 32 fp32 boxes (4 KiB each)
+constexpr int EPI_BOX_BYTES = 32 * 32 * 4;
+constexpr int EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /* align */ + 256 /* barriers */;
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 2 * BN;            // two accumulator buffers of BN fp32 columns
 constexpr int GROUP = 8;                          // tile-rows per rasterisation band
@@ -159,6 +170,7 @@ struct TcArgs {
   int a_bstride, b_bstride;   // split-operand rows between products (2M, 2N)
   int b_div;                  // product b reads B's product b / b_div
   int64_t c_bstride;          // C elements between products
+  int tma_c;                  // 1: epilogue through the C tensor map (batch 1, beta 0 or 1)
   int kmode;                  // triangular operand: K-steps a tile may skip (tile_krange)
   const unsigned *lo_nz;      // bit 0 / 1: A's / B's lo half has a nonzero (null: assume both)
 };
@@ -219,12 +231,31 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &ti,
   ti = r0 + jj + (int)u;
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory source of all but the newest bulk group has been read
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                              const __grid_constant__ CUtensorMap mapB,
+                                                             const __grid_constant__ CUtensorMap mapC,
                                                              const TcArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint8_t *epi = smem + STAGES * STAGE_BYTES;   // EPI_BYTES of staging, 1 KiB aligned
+  uint64_t *full = reinterpret_cast<uint64_t *>(epi + EPI_BYTES);
   uint64_t *empty = full + STAGES;
   uint64_t *tfull = empty + STAGES;   // [2] accumulator buffer complete
   uint64_t *tempty = tfull + 2;       // [2] accumulator buffer drained by the epilogue
@@ -342,6 +373,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   } else {
     // ---------------- epilogue (threads 64..191): TMEM lane quarter (warp % 4) -> rows
     const int quarter = warp & 3;
+    uint8_t *stg = epi + quarter * 2 * EPI_BOX_BYTES;   // this warp's two staging boxes
+    int boxes = 0;                                      // boxes this warp has handed to the TMA
     int lt = 0;
     for (int64_t t = blockIdx.x; t < args.ntiles; t += gridDim.x, lt++) {
       const int buf = lt & 1, use = lt >> 1;
@@ -375,7 +408,35 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       // the buffer's values are in registers: hand it back to the MMA warp
       asm volatile("tcgen05.fence::before_thread_sync;");
       mbar_arrive(&tempty[buf]);
-      if (row < args.M) {
+      if (args.tma_c) {
+        // rows >= M and columns >= N of a box lie outside the tensor map: the copy skips them
+        const float alpha = args.alpha;
+        const int y = ti * BM + quarter * 32;
+#pragma unroll
+        for (int c = 0; c < BN / 32; c++, boxes++) {
+          uint8_t *box = stg + (boxes & 1) * EPI_BOX_BYTES;
+          if (boxes >= 2) {   // the box's previous copy has finished reading it
+            if (lane == 0) bulk_wait_read_1();
+            __syncwarp();
+          }
+          // row `lane` of the box is 128 bytes; its 16-byte chunk q sits at chunk q ^ (lane & 7)
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const float4 v = make_float4(alpha * __uint_as_float(r[c * 32 + 4 * q + 0]),
+                                         alpha * __uint_as_float(r[c * 32 + 4 * q + 1]),
+                                         alpha * __uint_as_float(r[c * 32 + 4 * q + 2]),
+                                         alpha * __uint_as_float(r[c * 32 + 4 * q + 3]));
+            *reinterpret_cast<float4 *>(box + lane * 128 + ((q ^ (lane & 7)) << 4)) = v;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            if (args.beta == 0.0f) tma_store_2d(&mapC, box, (int)n0 + c * 32, y);
+            else tma_reduce_add_2d(&mapC, box, (int)n0 + c * 32, y);
+            bulk_commit();
+          }
+        }
+      } else if (row < args.M) {
         float *crow = args.C + b * args.c_bstride + row * args.ldc;
         const float alpha = args.alpha, beta = args.beta;
 #pragma unroll
@@ -411,6 +472,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
       }
     }
+    // every C box written before the CTA ends
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
@@ -460,6 +524,107 @@ __global__ void split_tf32_kernel(const float *__restrict__ src, int64_t ld, int
   if (lo_nz != nullptr && __syncthreads_or(lo_any) && tx == 0 && ty == 0) atomicOr(lo_nz, lo_bit);
 }
 
+__device__ __forceinline__ void split_store4(float *dst, int64_t R, int64_t r, int64_t kp, int64_t k, int64_t K,
+                                             float4 x, bool &lo_any) {
+  float4 hi, lo;
+  hi.x = __uint_as_float(__float_as_uint(x.x) & 0xffffe000u);
+  hi.y = __uint_as_float(__float_as_uint(x.y) & 0xffffe000u);
+  hi.z = __uint_as_float(__float_as_uint(x.z) & 0xffffe000u);
+  hi.w = __uint_as_float(__float_as_uint(x.w) & 0xffffe000u);
+  lo.x = __fsub_rn(x.x, hi.x);
+  lo.y = __fsub_rn(x.y, hi.y);
+  lo.z = __fsub_rn(x.z, hi.z);
+  lo.w = __fsub_rn(x.w, hi.w);
+  if (k + 3 < K) {
+    *reinterpret_cast<float4 *>(dst + r * kp + k) = hi;
+    *reinterpret_cast<float4 *>(dst + (R + r) * kp + k) = lo;
+    lo_any |= (lo.x != 0.0f) | (lo.y != 0.0f) | (lo.z != 0.0f) | (lo.w != 0.0f);
+  } else {
+    const float h4[4] = {hi.x, hi.y, hi.z, hi.w}, l4[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      if (k + j < K) {
+        dst[r * kp + k + j] = h4[j];
+        dst[(R + r) * kp + k + j] = l4[j];
+        lo_any |= l4[j] != 0.0f;
+      }
+  }
+}
+
+// The same split with 16-byte accesses, for sources whose rows start on 16
+// bytes (ld a multiple of 4, aligned base) and destinations with kp a
+// multiple of 4.  K-contiguous sources: one float4 of a row per thread, 32
+// rows x 128 K per block.  Transposed sources: 64 (K) x 64 (R) tiles through
+// shared memory, float4 loads along R and float4 stores along K.  Elements
+// past R or K are neither read nor written.
+template <bool KC>
+__global__ void __launch_bounds__(256) split_tf32_vec_kernel(const float *__restrict__ src, int64_t ld, int64_t R,
+                                                             int64_t K, int64_t src_bstride, float *__restrict__ dst,
+                                                             int64_t kp, unsigned *lo_nz, unsigned lo_bit) {
+  __shared__ float tile[KC ? 1 : 64][KC ? 1 : 65];
+  src += (int64_t)blockIdx.z * src_bstride;
+  dst += (int64_t)blockIdx.z * 2 * R * kp;
+  const int tid = threadIdx.x;
+  bool lo_any = false;
+  if (KC) {
+    const int64_t k = (int64_t)blockIdx.x * 128 + (tid & 31) * 4;
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      const int64_t r = (int64_t)blockIdx.y * 32 + p * 8 + (tid >> 5);
+      if (r >= R || k >= K) continue;
+      const float *sp = src + r * ld + k;
+      float4 x;
+      if (k + 3 < K) {
+        x = *reinterpret_cast<const float4 *>(sp);
+      } else {
+        x.x = sp[0];
+        x.y = k + 1 < K ? sp[1] : 0.0f;
+        x.z = k + 2 < K ? sp[2] : 0.0f;
+        x.w = 0.0f;
+      }
+      split_store4(dst, R, r, kp, k, K, x, lo_any);
+    }
+  } else {
+    const int64_t k0 = (int64_t)blockIdx.x * 64, r0 = (int64_t)blockIdx.y * 64;
+    {
+      const int rl = (tid & 15) * 4, kl = tid >> 4;   // 16 float4 along R, 16 K rows per pass
+      const int64_t r = r0 + rl;
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        const int kk = kl + 16 * p;
+        const int64_t k = k0 + kk;
+        float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (k < K && r < R) {
+          const float *sp = src + k * ld + r;
+          if (r + 3 < R) {
+            x = *reinterpret_cast<const float4 *>(sp);
+          } else {
+            x.x = sp[0];
+            x.y = r + 1 < R ? sp[1] : 0.0f;
+            x.z = r + 2 < R ? sp[2] : 0.0f;
+          }
+        }
+        tile[kk][rl + 0] = x.x;
+        tile[kk][rl + 1] = x.y;
+        tile[kk][rl + 2] = x.z;
+        tile[kk][rl + 3] = x.w;
+      }
+    }
+    __syncthreads();
+    const int kl = (tid & 15) * 4, rl = tid >> 4;   // 16 float4 along K, 16 rows per pass
+    const int64_t k = k0 + kl;
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      const int rr = rl + 16 * p;
+      const int64_t r = r0 + rr;
+      if (r >= R || k >= K) continue;
+      const float4 x = make_float4(tile[kl][rr], tile[kl + 1][rr], tile[kl + 2][rr], tile[kl + 3][rr]);
+      split_store4(dst, R, r, kp, k, K, x, lo_any);
+    }
+  }
+  if (lo_nz != nullptr && __syncthreads_or(lo_any) && tid == 0) atomicOr(lo_nz, lo_bit);
+}
+
 // ------------------------------------------------------------------ host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -493,6 +658,20 @@ static bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D fp32 tensor map over C (N columns x M rows, row stride ldc floats),
+// 32 x 32 boxes, 128-byte swizzle: the epilogue's bulk stores and reductions.
+static bool make_map_c(CUtensorMap *map, float *C, int64_t N, int64_t M, int64_t ldc) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)ldc * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 constexpr int kMaxDevices = 64;
 
 // Per device: SM count, and the stream-ordered pool the split operands come
@@ -517,8 +696,21 @@ static int device_sms(int dev) {
 
 int split_operand(const float *src, int64_t ld, int k_contig, int64_t R, int64_t K, int64_t src_bstride,
                   int batch, float *dst, int64_t kp, cudaStream_t s, unsigned *lo_nz, unsigned lo_bit) {
+  if (batch < 1 || batch > 65535) return HIF4X_ERR_UNSUPPORTED;
+  const bool vec = (ld & 3) == 0 && (src_bstride & 3) == 0 && (kp & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(src) & 15u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+  if (vec && k_contig && (R + 31) / 32 <= 65535) {
+    dim3 grid((unsigned)((K + 127) / 128), (unsigned)((R + 31) / 32), (unsigned)batch);
+    split_tf32_vec_kernel<true><<<grid, 256, 0, s>>>(src, ld, R, K, src_bstride, dst, kp, lo_nz, lo_bit);
+    return HIF4X_OK;
+  }
+  if (vec && !k_contig && (R + 63) / 64 <= 65535) {
+    dim3 grid((unsigned)((K + 63) / 64), (unsigned)((R + 63) / 64), (unsigned)batch);
+    split_tf32_vec_kernel<false><<<grid, 256, 0, s>>>(src, ld, R, K, src_bstride, dst, kp, lo_nz, lo_bit);
+    return HIF4X_OK;
+  }
   const int64_t gy = (R + 31) / 32;
-  if (gy > 65535 || batch < 1 || batch > 65535) return HIF4X_ERR_UNSUPPORTED;
+  if (gy > 65535) return HIF4X_ERR_UNSUPPORTED;
   dim3 grid((unsigned)((K + 31) / 32), (unsigned)gy, (unsigned)batch);
   split_tf32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, k_contig, R, K, src_bstride, dst, kp, lo_nz, lo_bit);
   return HIF4X_OK;
@@ -560,6 +752,13 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
   args.c_bstride = c_bstride;
   args.kmode = (kmode >= 0 && kmode <= 3) ? kmode : 0;
   args.lo_nz = lo_nz;
+  CUtensorMap mc{};
+  // N a multiple of 4: a bulk store past the tensor map's last column was seen
+  // to write up to the next 16-byte boundary, so C's row ends must fall on one
+  args.tma_c = (batch == 1 && args.vec && (N & 3) == 0 && (beta == 0.0f || beta == 1.0f) && M <= INT32_MAX &&
+                N <= INT32_MAX && make_map_c(&mc, C, N, M, ldc))
+                   ? 1
+                   : 0;
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
@@ -568,7 +767,7 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
   // Cholesky leaves and GPTQ column blocks of the same or another
   // calibration): a persistent grid on every SM holds them off until it ends
   const int64_t grid = std::min<int64_t>(args.ntiles, sms > 2 * kTcFreeSms ? sms - kTcFreeSms : sms);
-  gemm_tc_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, s>>>(ma, mb, args);
+  gemm_tc_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, args);
   return cudaGetLastError() == cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
 }
 

@@ -947,8 +947,12 @@ static int gemm_simt_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float a
                         int64_t ldc, int64_t strideC, int64_t batch, int lower, void *stream);
 
 // Products of at least this many multiply-adds go to the tensor cores;
-// smaller ones (per batch element) take the 32 x 32-tile SIMT kernel.
-static const int64_t kTcMinMacs = int64_t(1) << 27;
+// smaller ones (per batch element) take the SIMT kernels.  Measured alone on
+// one B200: 256 x 3968 x 128 (a GPTQ trailing update of 256 rows) 16 us on
+// the tensor cores against 32 us SIMT, 512 x 384 x 384 21 against 25 us;
+// 256^3 12 us SIMT against 18 us (the tensor-core call's two operand splits
+// and its launch dominate there).
+static const int64_t kTcMinMacs = int64_t(1) << 26;
 static const int64_t kSmallMaxMacs = int64_t(1) << 27;
 
 static int gemm_dispatch(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A, int64_t lda,

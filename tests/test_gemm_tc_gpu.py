@@ -122,3 +122,56 @@ def test_tc_gemm_tf32_exact_operands(exact):
     assert L.lib().hif4x_device_status(L.stream()) == L.OK
     err = float((got.double() - ref).abs().max() / ref.abs().max())
     assert err < 2e-6 * K ** 0.5 + 1e-6, err
+
+
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+@pytest.mark.parametrize("alpha", [1.0, -1.0, 0.375])
+def test_tc_gemm_bulk_epilogue_equals_register_epilogue(alpha, beta):
+    """With beta 0 or 1 and an aligned C the epilogue writes C by bulk tensor
+    stores (beta 0) or bulk add-reductions (beta 1, rounded to nearest);
+    with a C that is not 16-byte aligned it stores from registers
+    (fmaf(beta, C, v)).  The accumulators are the same, so the two results
+    must agree bit for bit, ragged edges included."""
+    M, N, K = 300, 200, 256
+    A, B = rnd(M, K, seed=31), rnd(K, N, seed=32)
+    C0 = rnd(M, N, seed=33)
+    # aligned C inside a larger buffer: the boxes past row M / column N must not be written
+    big = torch.full((320, 264), 7.0, device="cuda")
+    big[:M, :N] = C0
+    st = L.call("hif4x_gemm_tc", 0, 0, M, N, K, L.f32(alpha), L.ptr(A), K, L.ptr(B), N, L.f32(beta),
+                L.ptr(big), 264, L.stream())
+    assert st == L.OK
+    # the same product into a C that starts one float later (register epilogue)
+    big2 = torch.zeros(M, N + 3, device="cuda")
+    C2 = big2[:, 1:N + 1]
+    C2.copy_(C0)
+    st = L.call("hif4x_gemm_tc", 0, 0, M, N, K, L.f32(alpha), L.ptr(A), K, L.ptr(B), N, L.f32(beta),
+                L.ptr(C2), N + 3, L.stream())
+    assert st == L.OK
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    assert torch.equal(big[:M, :N], C2)
+    assert float((big[M:, :] - 7.0).abs().max()) == 0.0 and float((big[:, N:] - 7.0).abs().max()) == 0.0
+    ref = alpha * (A.double() @ B.double()) + beta * C0.double()
+    assert float((C2.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * K ** 0.5 + 1e-6
+
+
+@pytest.mark.parametrize("N", [133, 132])
+@pytest.mark.parametrize("ta,tb", [(0, 1), (1, 0)])
+def test_tc_gemm_split_ragged_tails(ta, tb, N):
+    """The 16-byte operand split with K and the row count not multiples of 4
+    (aligned leading dimensions): the K-contiguous form's K tail and the
+    transposing form's row tail are read and written element by element.
+    The columns of C past N stay untouched, with the bulk-store epilogue
+    (N = 132) and the register one (N = 133, not a multiple of 4)."""
+    M, K = 201, 299
+    Abig = rnd(K, 204, seed=34) if ta else rnd(M, 300, seed=34)
+    Bbig = rnd(N, 300, seed=35) if tb else rnd(K, 136, seed=35)
+    A = Abig[:, :M] if ta else Abig[:, :K]
+    B = Bbig[:, :K] if tb else Bbig[:, :N]
+    C = torch.zeros(M, 136, device="cuda")
+    st = L.call("hif4x_gemm_tc", ta, tb, M, N, K, L.f32(1.0), L.ptr(A), Abig.stride(0), L.ptr(B), Bbig.stride(0),
+                L.f32(0.0), L.ptr(C), 136, L.stream())
+    assert st == L.OK
+    ref = (A.double().T if ta else A.double()) @ (B.double().T if tb else B.double())
+    assert float((C[:, :N].double() - ref).abs().max() / ref.abs().max()) < 2e-6 * K ** 0.5 + 1e-6
+    assert float(C[:, N:].abs().max()) == 0.0

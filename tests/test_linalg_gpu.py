@@ -267,7 +267,7 @@ def test_gptq_production_size_vs_oracle(capsys):
 
 @pytest.mark.parametrize("T,C", [(50, 70), (700, 1000), (2048, 4160), (1, 33)])
 def test_gram_symmetric_vs_fp64(T, C):
-    """hif4x_gram: the lower tiles (tensor cores from 2^27 multiply-adds on,
+    """hif4x_gram: the lower tiles (tensor cores from 2^26 multiply-adds on,
     SIMT below) mirrored onto the upper triangle -- exactly symmetric, within
     the fp32-GEMM bound of X^T X, and accumulating into a given matrix."""
     X = rnd(T, C, seed=T + C)
