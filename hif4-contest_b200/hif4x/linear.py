@@ -9,6 +9,7 @@ the host RNG (torch.randperm after torch.manual_seed(0), solution.py:838,
 from __future__ import annotations
 
 import math
+import threading
 from typing import Any
 
 import torch
@@ -140,6 +141,62 @@ def _act_factor_finish(spec, stream):
     return Ua, order
 
 
+class SharedFactors:
+    """Transform-choice factors shared by calibrations of one weight set.
+
+    The factor of the transform choice (solution.py:884-896: the damped
+    Cholesky-inverse of the Hessian of the smoothed calibration samples but
+    the last, and the rotated space's factor derived from it) depends only
+    on the calibration list and on the smoothing exponent alpha: matrices that
+    take the same layer input (q/k/v_proj, gate/up_proj) and pick the same
+    alpha would compute the same factor, and every kernel on that path is
+    deterministic, so the first of them computes it and the others wait for
+    it on their streams (a CUDA event) instead of computing it again.
+
+    users: {id(calibration list): number of calibrations that will use it};
+    lists with one user are not cached.  An entry is dropped when the last
+    user of its list has passed its transform choice (release)."""
+
+    def __init__(self, users: dict):
+        self._lock = threading.Lock()
+        self._left = {k: v for k, v in users.items() if v > 1}
+        self._entries: dict = {}
+
+    def shares(self, calib) -> bool:
+        with self._lock:
+            return id(calib) in self._left
+
+    def get(self, calib, alpha: float, compute):
+        """compute() -> (CholLaunch, rotated factor, event recorded after both
+        on the computing stream), run by the first caller of (calib, alpha);
+        the others get its result once it is launched."""
+        key = (id(calib), alpha)
+        with self._lock:
+            ent = self._entries.get(key)
+            own = ent is None
+            if own:
+                ent = self._entries[key] = [threading.Event(), None]
+        if own:
+            try:
+                ent[1] = compute()
+            finally:
+                ent[0].set()
+            return ent[1]
+        ent[0].wait()
+        return ent[1] if ent[1] is not None else compute()   # the first caller failed: compute here
+
+    def release(self, calib) -> None:
+        with self._lock:
+            cid = id(calib)
+            if cid not in self._left:
+                return
+            self._left[cid] -= 1
+            if self._left[cid] <= 0:
+                del self._left[cid]
+                for key in [k for k in self._entries if k[0] == cid]:
+                    del self._entries[key]
+
+
 def _randperm(n: int, k: int, dev, rng: torch.Generator | None = None) -> torch.Tensor:
     """torch.randperm(n)[:k] on the host generator (the reference's RNG call)."""
     return torch.randperm(n, generator=rng)[:min(n, k)].to(dev)
@@ -193,7 +250,8 @@ def _refine_weight_values(w_final, q_used, weight_params: Dict5, calib_sm, mode)
 
 def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, calib_activation_list: list,
                      info: dict | None = None, return_device: bool = False,
-                     rng: torch.Generator | None = None, compact: bool = False) -> dict[str, Any]:
+                     rng: torch.Generator | None = None, compact: bool = False,
+                     shared: SharedFactors | None = None) -> dict[str, Any]:
     """hif4_calibration_and_quantize_weight (solution.py:826-1026).
 
     return_device=True keeps the weight parameters and the state tensors on the
@@ -202,7 +260,10 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     instead of re-seeding the global one (the same values; lets calibrations
     run concurrently from several threads).
     compact=True writes the compact activation state (compact_state): the
-    dynamic call rebuilds u_act / gw / gwf on the device, bit for bit."""
+    dynamic call rebuilds u_act / gw / gwf on the device, bit for bit.
+    shared: a SharedFactors of the weight set this matrix belongs to (the
+    transform-choice factor is then computed once per calibration list and
+    alpha); the results are the same."""
     if rng is None:
         torch.manual_seed(0)                                   # solution.py:838
     dev = _dev()
@@ -252,12 +313,27 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         # two GPTQ proxies then run on two streams; results are read after both
         main = torch.cuda.current_stream(dev)
         side = _side_stream(dev)
-        Hs = torch.zeros(C, C, dtype=torch.float32, device=dev)
-        for a in acts_s[:-1]:
-            la.gram(a, out=Hs, accumulate=True)
-        chol = la.chol_upper_inv_launch(Hs)
-        del Hs
-        factors = (chol.U, la.chol_rotate64(chol.U))
+
+        def factorise():
+            Hs = torch.zeros(C, C, dtype=torch.float32, device=dev)
+            for a in acts_s[:-1]:
+                la.gram(a, out=Hs, accumulate=True)
+            ch = la.chol_upper_inv_launch(Hs)
+            u1 = la.chol_rotate64(ch.U)
+            ev = torch.cuda.Event()
+            ev.record(main)
+            return ch, u1, ev
+
+        if shared is not None and shared.shares(calib_activation_list):
+            chol, U1, ev = shared.get(calib_activation_list, best_alpha, factorise)
+            main.wait_event(ev)
+            for t in (chol.U, U1):     # read on this calibration's streams too
+                t.record_stream(main)
+                t.record_stream(side)
+        else:
+            chol, U1, _ = factorise()
+        factors = (chol.U, U1)
+        del U1
         side.wait_stream(main)
         runs = []
         for md, stream in ((0, main), (1, side)):
@@ -281,6 +357,8 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         Uw = spaces[mode]
         spaces = None
         xh_pick = tf(xh_sub, mode)
+    if shared is not None:
+        shared.release(calib_activation_list)
 
     ph.mark("transform_choice")
     w_final = tf(w_s, mode)

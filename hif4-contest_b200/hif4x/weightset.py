@@ -43,8 +43,14 @@ def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None
     high-priority streams: the block scheduler gives their kernels the next
     free SMs, so the serial chains of a long matrix (the Cholesky leaves and
     GPTQ column blocks, one CTA each) do not queue behind the many-CTA
-    kernels of the shorter matrices beside it."""
+    kernels of the shorter matrices beside it.  Matrices whose jobs hold the
+    same calibration list object share their transform-choice factor when
+    they pick the same smoothing exponent (linear.SharedFactors)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    users: dict = {}
+    for job in jobs:
+        users[id(job[2])] = users.get(id(job[2]), 0) + 1
+    shared = linear.SharedFactors(users)
     out: dict = {}
     errors: list = []
     lock = threading.Lock()
@@ -63,7 +69,7 @@ def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None
             with torch.cuda.stream(_worker_stream(dev, i, key in urgent)):
                 try:
                     res = linear.calibrate_weight(wpair[0], wpair[1], calib, return_device=True,
-                                                  rng=torch.Generator().manual_seed(0))
+                                                  rng=torch.Generator().manual_seed(0), shared=shared)
                     dyn = None
                     if test is not None:
                         dyn = linear.dynamic_activation(test[0], test[1], res["activation_state"],

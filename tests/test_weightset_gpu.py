@@ -116,3 +116,36 @@ def test_convert_to_dir_resumes(tmp_path, monkeypatch):
         assert torch.equal(rec["packed"], shard.pack_params(ref["weight_params"]).cpu()), key
         assert rec["activation_state"]["mode"] == ref["activation_state"]["mode"]
         assert (rec["rows"], rec["cols"]) == tuple(wpair[0].shape)
+
+
+def test_shared_transform_factor_same_results():
+    """Matrices on one calibration list (as q/k/v_proj take one layer input)
+    converted together share the transform-choice factor of the alpha they
+    pick (linear.SharedFactors); every result equals a calibration of its
+    own, bit for bit."""
+    from hif4x import synth
+    _, calib, tests, _ = pc.linear_inputs("lin_c1024")
+    calib = [_dev(c) for c in calib]
+    test = _dev(tests[0])
+    C = int(calib[0][0].shape[1])
+    jobs = []
+    for i, N in enumerate((256, 384, 256, 128)):
+        w = synth.weight_c0(900 + i, N, C)
+        jobs.append((f"m{i}", _dev(list(synth.reference_form(*synth.quantize_nvfp4(w)))), calib, test))
+    info = {}
+    alphas = set()
+    for key, wpair, cal, _ in jobs:
+        linear.calibrate_weight(wpair[0], wpair[1], cal, info=info, return_device=True)
+        alphas.add(info["alpha"])
+    assert len(alphas) < len(jobs)   # at least two of them share a factor
+    got = weightset.convert(jobs, workers=3)
+    for key, wpair, cal, tst in jobs:
+        ref = linear.calibrate_weight(wpair[0], wpair[1], cal, return_device=True)
+        res, dyn = got[key]
+        for k in ref["weight_params"]:
+            assert torch.equal(res["weight_params"][k], ref["weight_params"][k]), (key, k)
+        for k in ("mode", "g", "tmax"):
+            assert res["activation_state"][k] == ref["activation_state"][k], (key, k)
+        dref = linear.dynamic_activation(tst[0], tst[1], ref["activation_state"], return_device=True)
+        for k in ("sf", "lv2", "lv3", "sign", "mant"):
+            assert torch.equal(getattr(dyn, k), getattr(dref, k)), (key, k)
