@@ -186,8 +186,10 @@ static int attention_tc(const float *Q, const float *K, const float *V, int64_t 
   const int64_t np = (int64_t)qh * 2 * T * kpt, nv = (int64_t)kvh * 2 * dh * kpt;
   float *ws = nullptr;
   if (cudaMallocAsync(reinterpret_cast<void **>(&ws), (size_t)(nq + nk + ns + np + nv) * sizeof(float), s) !=
-      cudaSuccess)
-    return HIF4X_ERR_LAUNCH;
+      cudaSuccess) {
+    cudaGetLastError();   // not sticky: clear it so later launch checks do not report it
+    return HIF4X_ERR_NOMEM;
+  }
   float *Qs = ws, *Ks = Qs + nq, *Sm = Ks + nk, *Ps = Sm + ns, *Vs = Ps + np;
   const int rep = qh / kvh;
   const float scale = 1.0f / sqrtf((float)dh);

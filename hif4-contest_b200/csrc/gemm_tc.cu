@@ -806,8 +806,10 @@ int hif4x_gemm_tc_ex(int ta, int tb, int64_t M, int64_t N, int64_t K, float alph
   float *ws = nullptr;
   // split operands, then one word: which operands have a nonzero lo half
   if (cudaMallocAsync(reinterpret_cast<void **>(&ws), (size_t)(a_floats + b_floats + 4) * sizeof(float), s) !=
-      cudaSuccess)
-    return HIF4X_ERR_LAUNCH;
+      cudaSuccess) {
+    cudaGetLastError();   // not sticky: clear it so later launch checks do not report it
+    return HIF4X_ERR_NOMEM;
+  }
   float *As = ws, *Bs = same ? ws : ws + a_floats;
   unsigned *lo_nz = reinterpret_cast<unsigned *>(ws + a_floats + b_floats);
   if (cudaMemsetAsync(lo_nz, 0, sizeof(unsigned), s) != cudaSuccess) {

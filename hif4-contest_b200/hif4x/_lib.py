@@ -15,7 +15,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 SO_PATH = os.path.join(_HERE, "libhif4x.so")
 
 OK, NOT_PD, TIMEOUT = 0, 1, 2
-ERR_ARG, ERR_LAUNCH, ERR_UNSUPPORTED, ERR_SCRATCH = -1, -2, -3, -4
+ERR_ARG, ERR_LAUNCH, ERR_UNSUPPORTED, ERR_SCRATCH, ERR_NOMEM = -1, -2, -3, -4, -5
 DT_F32, DT_BF16, DT_F64 = 0, 1, 2
 SRC_NVFP4_PACKED, SRC_NVFP4_PAIR, SRC_VALUES = 0, 1, 2
 SMOOTH_NONE, SMOOTH_MUL, SMOOTH_DIV = 0, 1, 2
@@ -23,7 +23,8 @@ ENC_NONE, ENC_SEARCH, ENC_FAST, ENC_ALG1 = 0, 1, 2, 3
 
 _STATUS = {OK: "ok", NOT_PD: "not positive definite", TIMEOUT: "device wait timed out",
            ERR_ARG: "bad argument", ERR_LAUNCH: "CUDA launch error", ERR_UNSUPPORTED: "unsupported",
-           ERR_SCRATCH: "size above the static scratch maximum"}
+           ERR_SCRATCH: "size above the static scratch maximum",
+           ERR_NOMEM: "out of device memory for a workspace"}
 
 
 class Hif4xError(RuntimeError):

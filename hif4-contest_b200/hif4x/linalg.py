@@ -118,6 +118,10 @@ class CholLaunch:
         self._keep = None
         return self.U if ok else None
 
+    def release(self) -> None:
+        """Drops the work buffers once the caller has read info itself."""
+        self._keep = None
+
 
 def chol_upper_inv_launch(H: torch.Tensor, damp: float = GPTQ_DAMP) -> CholLaunch:
     """chol_upper_inv on the current stream without synchronising it."""
@@ -237,6 +241,21 @@ def sq_sum_async(A: torch.Tensor) -> torch.Tensor:
 
 def abs_sum_f64(A: torch.Tensor) -> float:
     return _reduce(A, None, 1)
+
+
+def abs_sum_async(A: torch.Tensor) -> torch.Tensor:
+    """sum(|A|) in double as a one-element device tensor (no synchronisation)."""
+    out = torch.empty(1, dtype=torch.float64, device=A.device)
+    work = torch.empty(1024, dtype=torch.float64, device=A.device)
+    L.call("hif4x_reduce", L.ptr(A), None, A.numel(), 1, L.ptr(out), L.ptr(work), _s(A))
+    return out
+
+
+def read_scalars(*ts: torch.Tensor) -> list:
+    """The one-element device tensors ts as Python floats, read with a single
+    device-to-host copy (one synchronisation of the current stream instead of
+    one per value)."""
+    return torch.cat([t.reshape(1).double() for t in ts]).tolist()
 
 
 def diag(A: torch.Tensor) -> torch.Tensor:

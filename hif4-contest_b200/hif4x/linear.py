@@ -272,6 +272,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     w = decode_pair((weight_quant, weight_scale), dev)
     R, C = w.shape
     acts_raw = [decode_pair(p, dev) for p in calib_activation_list]
+    w_abs = la.abs_sum_async(w)          # the refinement gate's hash (read after the act-side guard)
     ph.mark("upload_decode")
 
     # ---- alpha smoothing search (solution.py:844-873)
@@ -286,11 +287,16 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     logm = la.smooth_logm(abs_sum, n_tok)
     rows = _randperm(R, 256, dev, rng)                         # solution.py:858
     w_rows = la.gather_rows(w, rows)
-    best_alpha, best_loss = 0.0, None
+    # the four losses are launched, then read with one synchronisation
+    sums = []
     for alpha in ALPHA_GRID:
         s = la.exp_scale(logm, alpha)
         wq = la.scale_cols(_encode_fast(w_rows, s)["deq"], s, L.SMOOTH_MUL)
-        loss = _resid_mse(a_big, wq, w_rows)
+        sums.append(la.sq_sum_async(_resid(a_big, wq, w_rows)))
+    n_loss = max(a_big.shape[0] * w_rows.shape[0], 1)
+    best_alpha, best_loss = 0.0, None
+    for alpha, sq in zip(ALPHA_GRID, la.read_scalars(*sums)):
+        loss = sq / n_loss                                      # la.mse: sum of squares / numel
         if best_loss is None or loss < best_loss:
             best_loss, best_alpha = loss, alpha
     s = la.exp_scale(logm, best_alpha)
@@ -345,12 +351,15 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         main.wait_stream(side)
         factors[1].record_stream(side)
         # a non-positive pivot in H0 is one in H1 = M^T H0 M as well (the same
-        # eigenvalues): both spaces take the reference's failed-factor branch
-        ok = chol.finish() is not None
+        # eigenvalues): both spaces take the reference's failed-factor branch;
+        # the pivot flag and both losses come back in one read
+        info0, sq0, sq1 = la.read_scalars(chol.info, runs[0][0], runs[1][0])
+        chol.release()
+        ok = info0 == 0
         spaces, cand = [], []
-        for U, (sq, n) in zip(factors, runs):
+        for U, sq, (_, n) in zip(factors, (sq0, sq1), runs):
             spaces.append(U if ok else None)
-            cand.append(float(sq.item()) / max(n, 1) if ok else float("inf"))
+            cand.append(sq / max(n, 1) if ok else float("inf"))
         mode = min(range(2), key=lambda i: (cand[i], i)) if not all(math.isnan(c) for c in cand) else 0
         if mode == 1 and spaces[1] is None:
             mode = 0
@@ -380,7 +389,8 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
         q_g = la.gptq(w_final, unit, Uw)
         res_r = _resid(xh_pick, q_used, w_final)
         res_g = _resid(xh_pick, q_g, w_final)
-        mse_r, mse_g = la.mse(res_r), la.mse(res_g)
+        mse_r, mse_g = (v / max(res_r.numel(), 1) for v in
+                        la.read_scalars(la.sq_sum_async(res_r), la.sq_sum_async(res_g)))
         res_q = res_r
         if mse_g < mse_r:
             weight_params = codec.values_to_params(q_g, weight_params)
@@ -410,8 +420,10 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
             # x' @ q^T - xh @ w^T = (x' - xh) @ q^T + xh @ (q - w)^T
             if res_q is None:
                 res_q = _resid(xh_pick, q_used, w_final)
-            mse_ar = la.mse(la.gemm(la.sub(xr, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone()))
-            mse_ag = la.mse(la.gemm(la.sub(xg, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone()))
+            r_ar = la.gemm(la.sub(xr, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone())
+            r_ag = la.gemm(la.sub(xg, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone())
+            mse_ar, mse_ag = (v / max(r_ar.numel(), 1) for v in
+                              la.read_scalars(la.sq_sum_async(r_ar), la.sq_sum_async(r_ag)))
             if mse_ag < mse_ar:
                 u_act = Ua
                 gptq_act = 1
@@ -420,7 +432,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
 
     ph.mark("act_gptq")
     # ---- weight lattice refinement and Gram carries (solution.py:986-1015)
-    e4h = int(la.abs_sum_f64(w) * 1e3) % 2 == 0
+    e4h = int(la.read_scalars(w_abs)[0] * 1e3) % 2 == 0
     e4 = C <= 4096
     tmax = REFINE_T_MAX if (C <= REFINE_MAX_C or e4h) else 512
     gw = gwf = None

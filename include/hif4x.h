@@ -43,6 +43,9 @@ extern "C" {
 #define HIF4X_ERR_LAUNCH (-2)     /* CUDA launch or runtime error             */
 #define HIF4X_ERR_UNSUPPORTED (-3)
 #define HIF4X_ERR_SCRATCH (-4)    /* size above a static scratch maximum      */
+#define HIF4X_ERR_NOMEM (-5)      /* a stream-ordered workspace (the tensor-core
+                                     GEMM's split operands, the attention's
+                                     buffers) could not be allocated          */
 
 /* ---- enums ------------------------------------------------------------- */
 #define HIF4X_DT_F32 0

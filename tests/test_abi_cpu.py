@@ -21,6 +21,15 @@ from conftest import ROOT
 L = pytest.importorskip("hif4x._lib")
 
 
+def test_status_codes_match_header():
+    """The binding's status constants are the header's #defines."""
+    txt = open(os.path.join(ROOT, "include", "hif4x.h")).read()
+    defs = {m[0]: int(m[1]) for m in re.findall(r"#define HIF4X_(\w+) \(?(-?\d+)\)?", txt)}
+    for name in ("OK", "NOT_PD", "TIMEOUT", "ERR_ARG", "ERR_LAUNCH", "ERR_UNSUPPORTED", "ERR_SCRATCH", "ERR_NOMEM"):
+        assert defs[name] == getattr(L, name), name
+        assert getattr(L, name) in L._STATUS
+
+
 def declared_symbols() -> list[str]:
     names = []
     for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
