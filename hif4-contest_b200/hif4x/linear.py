@@ -129,18 +129,6 @@ def _act_factor_launch(q: torch.Tensor):
     return Ha, order, la.chol_upper_inv_launch(la.permute_sym(Ha, order))
 
 
-def _act_factor_finish(spec, stream):
-    """(Ua, order) from _act_factor_launch; the unpermuted factorisation when
-    the permuted one is not positive definite, as the reference falls back."""
-    Ha, order, chol = spec
-    Ua = chol.finish()
-    if Ua is None:
-        return la.chol_upper_inv(Ha), None
-    Ua.record_stream(stream)
-    order.record_stream(stream)
-    return Ua, order
-
-
 class SharedFactors:
     """Transform-choice factors shared by calibrations of one weight set.
 
@@ -404,35 +392,51 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
 
     # ---- activation-side GPTQ with act-order (solution.py:936-976)
     u_act, gptq_act, order = None, 0, None
+    w_abs_v = None
     if xh_pick is not None:
         main = torch.cuda.current_stream(dev)
         main.wait_stream(_side_stream(dev))
         if spec is None or gptq_w:
             spec = _act_factor_launch(q_used)
-        Ua, order = _act_factor_finish(spec, main)
+        Ha, order_p, chol = spec
         spec = None
-        if Ua is not None:
-            p_r, xr, unit_x = _search(xh_pick)
-            if order is not None:
-                xg = la.scatter_cols(la.gptq(la.gather_cols(xh_pick, order), la.gather_cols(unit_x, order), Ua), order)
+        chol.U.record_stream(main)
+        order_p.record_stream(main)
+        p_r, xr, unit_x = _search(xh_pick)
+        # x' @ q^T - xh @ w^T = (x' - xh) @ q^T + xh @ (q - w)^T
+        if res_q is None:
+            res_q = _resid(xh_pick, q_used, w_final)
+        r_ar = la.gemm(la.sub(xr, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone())
+        n_act = max(r_ar.numel(), 1)
+
+        def act_gptq_sq(Ua, order_):
+            if order_ is not None:
+                xg = la.scatter_cols(la.gptq(la.gather_cols(xh_pick, order_), la.gather_cols(unit_x, order_), Ua),
+                                     order_)
             else:
                 xg = la.gptq(xh_pick, unit_x, Ua)
-            # x' @ q^T - xh @ w^T = (x' - xh) @ q^T + xh @ (q - w)^T
-            if res_q is None:
-                res_q = _resid(xh_pick, q_used, w_final)
-            r_ar = la.gemm(la.sub(xr, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone())
-            r_ag = la.gemm(la.sub(xg, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone())
-            mse_ar, mse_ag = (v / max(r_ar.numel(), 1) for v in
-                              la.read_scalars(la.sq_sum_async(r_ar), la.sq_sum_async(r_ag)))
-            if mse_ag < mse_ar:
-                u_act = Ua
-                gptq_act = 1
-            else:
-                order = None
+            return la.sq_sum_async(la.gemm(la.sub(xg, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone()))
+
+        # the permuted factor is used before its pivot flag is read: the flag,
+        # both losses and the refinement gate's hash come back in one read
+        sq_ag = act_gptq_sq(chol.U, order_p)
+        info_a, sq_ar_v, sq_ag_v, w_abs_v = la.read_scalars(chol.info, la.sq_sum_async(r_ar), sq_ag, w_abs)
+        chol.release()
+        Ua, order = chol.U, order_p
+        if info_a != 0:
+            # a non-positive pivot: the reference's fallback, the unpermuted factorisation
+            Ua, order = la.chol_upper_inv(Ha), None
+            if Ua is not None:
+                sq_ag_v = la.read_scalars(act_gptq_sq(Ua, None))[0]
+        if Ua is not None and sq_ag_v / n_act < sq_ar_v / n_act:
+            u_act = Ua
+            gptq_act = 1
+        else:
+            order = None
 
     ph.mark("act_gptq")
     # ---- weight lattice refinement and Gram carries (solution.py:986-1015)
-    e4h = int(la.read_scalars(w_abs)[0] * 1e3) % 2 == 0
+    e4h = int((w_abs_v if w_abs_v is not None else la.read_scalars(w_abs)[0]) * 1e3) % 2 == 0
     e4 = C <= 4096
     tmax = REFINE_T_MAX if (C <= REFINE_MAX_C or e4h) else 512
     gw = gwf = None
