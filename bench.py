@@ -734,7 +734,9 @@ def run_gemm(args, rank, ws, local_rank):
     full NT product (hif4x_gemm, 8192^3) -- against the tensor roofline.  The
     3xTF32 scheme issues three TF32 MMAs per fp32-equivalent multiply-add;
     the measured dense bf16 peak (MEASURED_PEAKS.json) bounds TF32 at half of
-    it, so the fp32-equivalent roofline is bf16 / 6."""
+    it, so the fp32-equivalent roofline is bf16 / 6.  A GPTQ trailing update
+    (C -= E U, K = 128, down_proj's weight GPTQ at 10752 remaining columns)
+    is bound by HBM instead: C read and written, E and U read once."""
     import torch
 
     from hif4x import linalg as la
@@ -753,19 +755,33 @@ def run_gemm(args, rank, ws, local_rank):
     G = torch.empty(14336, 14336, device=dev)
     Cm = torch.empty(8192, 8192, device=dev)
     H1 = la.gram(X[:, :4096].contiguous())
+    E = torch.randn(4096, 128, device=dev, generator=g)
+    Ub = torch.randn(128, 10752, device=dev, generator=g) * 1e-3
+    Wt = torch.randn(4096, 10752, device=dev, generator=g)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            hbm = float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        hbm = 6650.0
     cases = {
         "gram 6144 x 14336 (lower tiles + mirror)": (lambda: la.gram(X, out=G), 6144 * 14336 * 14336.0),
         "gemm NT 8192^3": (lambda: la.gemm(A, B, tb=True, out=Cm), 2.0 * 8192 ** 3),
         # the Cholesky-inverse: n^3/3 multiply-adds for the factor and n^3/3 for the inverse
         "chol_upper_inv n = 14336": (lambda: la.chol_upper_inv(G), 2.0 * 14336 ** 3 / 3),
         "chol_upper_inv n = 4096": (lambda: la.chol_upper_inv(H1), 2.0 * 4096 ** 3 / 3),
+        "gptq trailing update 4096 x 10752 x 128 (C -= E U)":
+            (lambda: la.gemm(E, Ub, alpha=-1.0, beta=1.0, out=Wt), 2.0 * 4096 * 10752 * 128),
     }
+    hbm_bytes = {"gptq trailing update 4096 x 10752 x 128 (C -= E U)":
+                 4.0 * (2 * 4096 * 10752 + 4096 * 128 + 128 * 10752)}
     clk = ClockSampler(physical_gpu(local_rank))
     clk.start()
     time.sleep(0.3)
     out = {}
     la.gram(X, out=G)   # a Hessian for the Cholesky cases
     for name, (fn, flops) in cases.items():
+        if args.case and args.case not in name:
+            continue
         for _ in range(max(3, args.warmup)):
             fn()
         torch.cuda.synchronize(dev)
@@ -781,6 +797,10 @@ def run_gemm(args, rank, ws, local_rank):
         tfs = flops / (ms * 1e-3) / 1e12
         out[name] = {"ms": ms, "fp32_equiv_tflops": tfs, "roofline_tflops": bf16 / 6, "frac": tfs / (bf16 / 6),
                      "clocks": clk.summary(w0, w1)}
+        if name in hbm_bytes:   # memory-bound: HBM roofline on the algorithmic bytes
+            gbs = hbm_bytes[name] / (ms * 1e-3) / 1e9
+            out[name].update({"bound": "hbm", "alg_bytes": hbm_bytes[name], "achieved_gbs": gbs,
+                              "peak_gbs": hbm, "frac": gbs / hbm})
     clk.stop()
     if rank != 0:
         return
@@ -912,6 +932,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention", "matrix", "gemm"])
     ap.add_argument("--matrix", default="down_proj", help="matrix workload: Llama-3-8B layer matrix name")
+    ap.add_argument("--case", default="", help="gemm workload: run only the cases whose name contains this")
     ap.add_argument("--tokens", type=int, default=8192,
                     help="matrix workload: calibration tokens (4 samples; 8192 as the weight set, 4096 as one layer)")
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
