@@ -941,9 +941,9 @@ def main():
     ap.add_argument("--pipeline-layers", type=int, default=32,
                     help="codec workload: decoder layers of the weight-set object (32 = the full weight set)")
     ap.add_argument("--pipeline-steps", type=int, default=2, help="timed conversions of the weight set")
-    ap.add_argument("--pipeline-warmup", type=int, default=2,
+    ap.add_argument("--pipeline-warmup", type=int, default=3,
                     help="untimed conversions of the weight set first (the first ones after start-up still "
-                         "grow the allocator's pools)")
+                         "grow the allocator's pools: 443, 86, 29, then 2-9 device allocations per conversion)")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "codec":
         args.warmup = 3
