@@ -43,16 +43,32 @@
 namespace hif4x {
 namespace tc {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
-constexpr int TILE_BYTES = BM * BK * 4;           // 16 KiB (A and B tiles are the same size)
-constexpr int STAGE_BYTES = 4 * TILE_BYTES;        // A hi, A lo, B hi, B lo
+constexpr int BM = 128, BK = 32;
+constexpr int TILE_A_BYTES = BM * BK * 4;          // 16 KiB per A half (hi or lo) and stage
 // epilogue staging: per epilogue warp two 32 x 32 fp32 boxes (4 KiB each)
 constexpr int EPI_BOX_BYTES = 32 * 32 * 4;
 constexpr int EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /* align */ + 256 /* barriers */;
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 2 * BN;            // two accumulator buffers of BN fp32 columns
 constexpr int GROUP = 8;                          // tile-rows per rasterisation band
+
+// Output tiles are BM x BN_ with BN_ 128 or 256 (one tcgen05.mma of N = BN_).
+// A 128 x 128 MMA reads 8 KiB of operands from shared memory per 128x128x8
+// step while the TMA writes as much again, which holds the tensor pipe near
+// 70 %; N = 256 reads 12 KiB per twice the work.  The wider tile has two
+// stages of 96 KiB (A hi, A lo, B hi, B lo), the narrow one three of 64 KiB,
+// so both take the same shared memory; TMEM holds two accumulator buffers of
+// BN_ fp32 columns (512 of 512 columns for BN_ = 256).
+template <int BN_>
+struct Tile {
+  static constexpr int BN = BN_;
+  static constexpr int STAGES = BN_ == 256 ? 2 : 3;
+  static constexpr int TILE_B = BN_ * BK * 4;
+  static constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /* align */ + 256 /* barriers */;
+  static constexpr uint32_t TMEM_COLS = 2 * BN_;
+};
+static_assert(Tile<128>::SMEM_BYTES <= 232448 && Tile<256>::SMEM_BYTES <= 232448, "shared memory per CTA");
+static_assert(Tile<256>::TMEM_COLS <= 512, "tensor memory columns");
 constexpr long long SPIN_LIMIT = 1ll << 22;
 // SMs a persistent GEMM leaves free: 16 of 148 took down_proj's calibration
 // (tensor-core Grams and Cholesky products beside one-CTA leaves and GPTQ
@@ -129,10 +145,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
-// Instruction descriptor: D fp32, A/B tf32, M = 128, N = 128, majors.
+// Instruction descriptor: D fp32, A/B tf32, M = 128, N = BN_, majors.
+template <int BN_>
 __host__ __device__ constexpr uint32_t instr_desc(int a_mn_major, int b_mn_major) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn_major << 15) | ((uint32_t)b_mn_major << 16) |
-         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(BN_ >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -163,7 +180,7 @@ struct TcArgs {
   int64_t ldc;
   int a_lo, b_lo;   // row of the lo half in each split operand (hi rows come first)
   int tm, tn;       // tile rows / columns of one product
-  int lower;        // 1: only tiles on or below the diagonal (square C)
+  int lower;        // 1: only tiles reaching the diagonal or below it (square C)
   int vec;          // 1: C rows take 16-byte stores
   int64_t ntiles;   // batch * tiles_per
   int64_t tiles_per;
@@ -178,23 +195,27 @@ struct TcArgs {
 // K-steps [kb, ke) that can be nonzero for output tile (ti, tj) when one
 // operand is triangular (its other entries are zeros in memory, so skipping
 // them only saves work):
-//   kmode 1: B(n, k) = 0 for k > n  ->  k < (tj + 1) * BN
-//   kmode 2: B(n, k) = 0 for k < n  ->  k >= tj * BN
+//   kmode 1: B(n, k) = 0 for k > n  ->  k < (tj + 1) * BN_
+//   kmode 2: B(n, k) = 0 for k < n  ->  k >= tj * BN_
 //   kmode 3: A(m, k) = 0 for k > m  ->  k < (ti + 1) * BM
 // At least one step is always kept, so every accumulator is written.
+template <int BN_>
 __device__ __forceinline__ void tile_krange(const TcArgs &a, int ti, int tj, int nk, int &kb, int &ke) {
   kb = 0;
   ke = nk;
-  if (a.kmode == 1) ke = min(nk, (tj + 1) * (BN / BK));
-  else if (a.kmode == 2) kb = min(nk - 1, tj * (BN / BK));
+  if (a.kmode == 1) ke = min(nk, (tj + 1) * (BN_ / BK));
+  else if (a.kmode == 2) kb = min(nk - 1, tj * (BN_ / BK));
   else if (a.kmode == 3) ke = min(nk, (ti + 1) * (BM / BK));
 }
 
 // Tile t of the visiting order -> (tile row, tile column).  Bands of GROUP
-// tile-rows; inside a band, column by column.  With `lower` (tm == tn) only
-// tiles with column <= row exist: band b holds rows [bG, bG+g), each row i
-// with columns 0..i, so the band is a g-wide rectangle of bG columns followed
-// by a g-row triangle.
+// tile-rows; inside a band, column by column.  With `lower` (M == N) only the
+// tiles that reach the diagonal or lie below it exist: with R = BN_ / BM
+// (1 or 2) row ti has columns 0 .. ti / R, and column p starts at row R p.
+// In band b (rows [r0, r0 + g), r0 = bG) the columns p <= r0 / R have all g
+// rows, the later ones r0 + g - R p rows.  A tile that crosses the diagonal is
+// computed whole (its entries above the diagonal are written too).
+template <int BN_>
 __device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &ti, int &tj) {
   if (!a.lower) {
     const int64_t per_band = (int64_t)GROUP * a.tn;
@@ -205,30 +226,44 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &ti,
     ti = band * GROUP + (int)(r % g);
     return;
   }
+  constexpr int R = BN_ / BM;
   int band = 0;
   int64_t start = 0;
   for (;;) {
     const int r0 = band * GROUP, g = min(GROUP, a.tm - r0);
-    const int64_t size = (int64_t)g * r0 + (int64_t)g * (g + 1) / 2;
+    const int p0 = r0 / R + 1, pmax = (r0 + g - 1) / R;   // full columns 0 .. p0-1
+    int64_t size = (int64_t)p0 * g;
+    for (int p = p0; p <= pmax; p++) size += r0 + g - R * p;
     if (t < start + size) break;
     start += size;
     band++;
   }
   const int r0 = band * GROUP, g = min(GROUP, a.tm - r0);
+  const int p0 = r0 / R + 1;
   int64_t u = t - start;
-  if (u < (int64_t)r0 * g) {
+  if (u < (int64_t)p0 * g) {
     tj = (int)(u / g);
     ti = r0 + (int)(u % g);
     return;
   }
-  u -= (int64_t)r0 * g;
-  int jj = 0;
-  while (u >= g - jj) {
-    u -= g - jj;
-    jj++;
+  u -= (int64_t)p0 * g;
+  int p = p0;
+  while (u >= r0 + g - R * p) {
+    u -= r0 + g - R * p;
+    p++;
   }
-  tj = r0 + jj;
-  ti = r0 + jj + (int)u;
+  tj = p;
+  ti = R * p + (int)u;
+}
+
+// Number of tiles of one product in the order above.
+template <int BN_>
+static int64_t tiles_of(int tm, int tn, int lower) {
+  if (!lower) return (int64_t)tm * tn;
+  constexpr int R = BN_ / BM;
+  int64_t n = 0;
+  for (int ti = 0; ti < tm; ti++) n += ti / R + 1;
+  return n;
 }
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
@@ -248,10 +283,14 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+template <int BN_>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                              const __grid_constant__ CUtensorMap mapB,
                                                              const __grid_constant__ CUtensorMap mapC,
                                                              const TcArgs args) {
+  using Cfg = Tile<BN_>;
+  constexpr int BN = BN_, STAGES = Cfg::STAGES, STAGE_BYTES = Cfg::STAGE_BYTES, TILE_B = Cfg::TILE_B;
+  constexpr uint32_t TMEM_COLS = Cfg::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *epi = smem + STAGES * STAGE_BYTES;   // EPI_BYTES of staging, 1 KiB aligned
@@ -271,7 +310,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   // the same word, so they agree on the stage layout.
   const unsigned lz = args.lo_nz != nullptr ? *args.lo_nz : 3u;
   const bool a_lo_on = (lz & 1u) != 0u, b_lo_on = (lz & 2u) != 0u;
-  const uint32_t stage_tx = (uint32_t)TILE_BYTES * (2u + (a_lo_on ? 1u : 0u) + (b_lo_on ? 1u : 0u));
+  const uint32_t stage_tx =
+      (uint32_t)TILE_A_BYTES * (a_lo_on ? 2u : 1u) + (uint32_t)TILE_B * (b_lo_on ? 2u : 1u);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -304,20 +344,21 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       for (int64_t t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x) {
         const int64_t b = t / args.tiles_per;
         int ti, tj;
-        tile_coords(args, t - b * args.tiles_per, ti, tj);
+        tile_coords<BN>(args, t - b * args.tiles_per, ti, tj);
         const int m0 = (int)b * args.a_bstride + ti * BM, n0 = (int)(b / args.b_div) * args.b_bstride + tj * BN;
         int kb, ke;
-        tile_krange(args, ti, tj, nk, kb, ke);
+        tile_krange<BN>(args, ti, tj, nk, kb, ke);
         for (int kt = kb; kt < ke; kt++, g++) {
           const int s = (int)(g % STAGES);
           if (g >= STAGES) ok = mbar_wait(&empty[s], (uint32_t)(((g / STAGES) - 1) & 1));
           if (!ok) break;
           uint8_t *st = smem + s * STAGE_BYTES;
           mbar_expect_tx(&full[s], stage_tx);
+          // stage layout: A hi, A lo (TILE_A_BYTES each), B hi, B lo (TILE_B each)
           tma_load_2d(&mapA, st, &full[s], kt * BK, m0);
-          if (a_lo_on) tma_load_2d(&mapA, st + TILE_BYTES, &full[s], kt * BK, args.a_lo + m0);
-          tma_load_2d(&mapB, st + 2 * TILE_BYTES, &full[s], kt * BK, n0);
-          if (b_lo_on) tma_load_2d(&mapB, st + 3 * TILE_BYTES, &full[s], kt * BK, args.b_lo + n0);
+          if (a_lo_on) tma_load_2d(&mapA, st + TILE_A_BYTES, &full[s], kt * BK, args.a_lo + m0);
+          tma_load_2d(&mapB, st + 2 * TILE_A_BYTES, &full[s], kt * BK, n0);
+          if (b_lo_on) tma_load_2d(&mapB, st + 2 * TILE_A_BYTES + TILE_B, &full[s], kt * BK, args.b_lo + n0);
         }
       }
       // drain: every issued copy has landed before the CTA may exit (the
@@ -329,7 +370,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(0, 0);
+      const uint32_t idesc = instr_desc<BN>(0, 0);
       int64_t g = 0;
       int lt = 0;
       for (int64_t t = blockIdx.x; t < args.ntiles && ok; t += gridDim.x, lt++) {
@@ -342,8 +383,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         if (args.kmode != 0) {
           const int64_t b = t / args.tiles_per;
           int ti, tj;
-          tile_coords(args, t - b * args.tiles_per, ti, tj);
-          tile_krange(args, ti, tj, nk, kb, ke);
+          tile_coords<BN>(args, t - b * args.tiles_per, ti, tj);
+          tile_krange<BN>(args, ti, tj, nk, kb, ke);
         }
         for (int kt = kb; kt < ke; kt++, g++) {
           const int s = (int)(g % STAGES);
@@ -351,8 +392,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           if (!ok) break;
           asm volatile("tcgen05.fence::after_thread_sync;");
           const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t a_hi = base, a_lo = base + TILE_BYTES;
-          const uint32_t b_hi = base + 2 * TILE_BYTES, b_lo = base + 3 * TILE_BYTES;
+          const uint32_t a_hi = base, a_lo = base + TILE_A_BYTES;
+          const uint32_t b_hi = base + 2 * TILE_A_BYTES, b_lo = base + 2 * TILE_A_BYTES + TILE_B;
 #pragma unroll
           for (int j = 0; j < BK / 8; j++) {
             const uint64_t dah = kmajor_desc(a_hi, j), dal = kmajor_desc(a_lo, j);
@@ -384,13 +425,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       asm volatile("tcgen05.fence::after_thread_sync;");
       const int64_t b = t / args.tiles_per;
       int ti, tj;
-      tile_coords(args, t - b * args.tiles_per, ti, tj);
+      tile_coords<BN>(args, t - b * args.tiles_per, ti, tj);
       const int64_t row = (int64_t)ti * BM + quarter * 32 + lane;
-      const int64_t n0 = (int64_t)tj * BN;
-      uint32_t r[BN];
+      // 128 accumulator columns at a time (BN / 128 halves); the buffer goes
+      // back to the MMA warp once the last of them is in registers
+#pragma unroll 1
+      for (int h = 0; h < BN / 128; h++) {
+      const int64_t n0 = (int64_t)tj * BN + h * 128;
+      uint32_t r[128];
 #pragma unroll
-      for (int c = 0; c < BN / 32; c++) {
-        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c * 32);
+      for (int c = 0; c < 4; c++) {
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + h * 128 + c * 32);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
             "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
@@ -405,15 +450,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             : "r"(taddr));
       }
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      // the buffer's values are in registers: hand it back to the MMA warp
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      mbar_arrive(&tempty[buf]);
+      if (h == BN / 128 - 1) {
+        // the buffer's values are in registers: hand it back to the MMA warp
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        mbar_arrive(&tempty[buf]);
+      }
       if (args.tma_c) {
         // rows >= M and columns >= N of a box lie outside the tensor map: the copy skips them
         const float alpha = args.alpha;
         const int y = ti * BM + quarter * 32;
 #pragma unroll
-        for (int c = 0; c < BN / 32; c++, boxes++) {
+        for (int c = 0; c < 4; c++, boxes++) {
           uint8_t *box = stg + (boxes & 1) * EPI_BOX_BYTES;
           if (boxes >= 2) {   // the box's previous copy has finished reading it
             if (lane == 0) bulk_wait_read_1();
@@ -440,7 +487,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         float *crow = args.C + b * args.c_bstride + row * args.ldc;
         const float alpha = args.alpha, beta = args.beta;
 #pragma unroll
-        for (int c = 0; c < BN / 32; c++) {
+        for (int c = 0; c < 4; c++) {
           const int64_t col0 = n0 + c * 32;
           if (args.vec && col0 + 32 <= args.N) {
             float4 *dst = reinterpret_cast<float4 *>(crow + col0);
@@ -471,6 +518,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           }
         }
       }
+      }   // halves
     }
     // every C box written before the CTA ends
     if (lane == 0) bulk_wait_all();
@@ -644,14 +692,15 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2-D fp32 tensor map over a split operand: `inner` (K) x `outer` (2R) floats,
-// row stride ld floats, 32 x 128 boxes, 128-byte swizzle; K beyond `inner`
-// reads as zero.
-static bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld) {
+// row stride ld floats, 32 x box_rows boxes, 128-byte swizzle; K beyond
+// `inner` reads as zero.
+static bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld,
+                     int box_rows = BM) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -727,8 +776,16 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
   if (cudaGetDevice(&dev) != cudaSuccess) return HIF4X_ERR_LAUNCH;
   const int sms = device_sms(dev);
   if (sms <= 0) return HIF4X_ERR_LAUNCH;
+  const int lower_ok = (lower && M == N) ? 1 : 0;
+  const int tm = (int)((M + BM - 1) / BM);
+  // 128 x 256 tiles for long products that still fill two waves of CTAs with
+  // them; the 128 x 128 tiles otherwise (short K is bound by C's traffic, and
+  // small products need the CTA count)
+  const int64_t cap = sms > 2 * kTcFreeSms ? sms - kTcFreeSms : sms;
+  const bool wide = K >= 512 && tiles_of<256>(tm, (int)((N + 255) / 256), lower_ok) * batch >= 2 * cap;
+  const int bn = wide ? 256 : 128;
   CUtensorMap ma, mb;
-  if (!make_map(&ma, As, K, 2 * M * a_products, kp) || !make_map(&mb, Bs, K, 2 * N * b_products, kp))
+  if (!make_map(&ma, As, K, 2 * M * a_products, kp) || !make_map(&mb, Bs, K, 2 * N * b_products, kp, bn))
     return HIF4X_ERR_UNSUPPORTED;
   TcArgs args{};
   args.M = M;
@@ -740,11 +797,11 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
   args.ldc = ldc;
   args.a_lo = (int)M;
   args.b_lo = (int)N;
-  args.tm = (int)((M + BM - 1) / BM);
-  args.tn = (int)((N + BN - 1) / BN);
-  args.lower = (lower && M == N) ? 1 : 0;
+  args.tm = tm;
+  args.tn = (int)((N + bn - 1) / bn);
+  args.lower = lower_ok;
   args.vec = ((ldc & 3) == 0 && (c_bstride & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0) ? 1 : 0;
-  args.tiles_per = args.lower ? (int64_t)args.tm * (args.tm + 1) / 2 : (int64_t)args.tm * args.tn;
+  args.tiles_per = wide ? tiles_of<256>(args.tm, args.tn, args.lower) : tiles_of<128>(args.tm, args.tn, args.lower);
   args.ntiles = args.tiles_per * batch;
   args.a_bstride = (int)(2 * M);
   args.b_bstride = (int)(2 * N);
@@ -761,13 +818,17 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
                    : 0;
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<128>::SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<256>::SMEM_BYTES);
   });
   // leave kTcFreeSms SMs to the latency-bound kernels of other streams (the
   // Cholesky leaves and GPTQ column blocks of the same or another
   // calibration): a persistent grid on every SM holds them off until it ends
-  const int64_t grid = std::min<int64_t>(args.ntiles, sms > 2 * kTcFreeSms ? sms - kTcFreeSms : sms);
-  gemm_tc_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, args);
+  const int64_t grid = std::min<int64_t>(args.ntiles, cap);
+  if (wide)
+    gemm_tc_kernel<256><<<(unsigned)grid, THREADS, Tile<256>::SMEM_BYTES, s>>>(ma, mb, mc, args);
+  else
+    gemm_tc_kernel<128><<<(unsigned)grid, THREADS, Tile<128>::SMEM_BYTES, s>>>(ma, mb, mc, args);
   return cudaGetLastError() == cudaSuccess ? HIF4X_OK : HIF4X_ERR_LAUNCH;
 }
 

@@ -175,3 +175,42 @@ def test_tc_gemm_split_ragged_tails(ta, tb, N):
     ref = (A.double().T if ta else A.double()) @ (B.double().T if tb else B.double())
     assert float((C[:, :N].double() - ref).abs().max() / ref.abs().max()) < 2e-6 * K ** 0.5 + 1e-6
     assert float(C[:, N:].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("ta,tb,alpha,beta", [(0, 1, 1.0, 0.0), (1, 0, -1.0, 1.0), (0, 0, 0.5, 0.0)])
+@pytest.mark.parametrize("M,N,K", [(4096, 2304, 512), (4100, 2300, 520)])
+def test_tc_gemm_wide_tiles_vs_fp64(M, N, K, ta, tb, alpha, beta):
+    """Products long enough (K >= 512) and with at least two waves of 128 x 256
+    output tiles take the wide-tile kernel (one N = 256 MMA per step, two
+    96 KiB stages, 512 TMEM columns): ragged M, N and K tails, both epilogues
+    (beta 0 stores, beta 1 add-reductions), against float64."""
+    A = rnd(K, M, seed=41) if ta else rnd(M, K, seed=41)
+    B = rnd(N, K, seed=42) if tb else rnd(K, N, seed=42)
+    C0 = rnd(M, N, seed=43)
+    ref = alpha * ((A.double().T if ta else A.double()) @ (B.double().T if tb else B.double())) + beta * C0.double()
+    got = tc_gemm(A, B, ta, tb, alpha=alpha, beta=beta, C=C0.clone())
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    err = float((got.double() - ref).abs().max() / ref.abs().max())
+    assert err < 2e-6 * K ** 0.5 + 1e-6, err
+
+
+def test_tc_gemm_wide_tiles_untouched_outside():
+    """The wide-tile kernel writes nothing past row M or column N of C, with
+    the bulk epilogue (aligned C) and the register one (C one float off)."""
+    M, N, K = 4100, 2300, 512
+    A, B = rnd(M, K, seed=44), rnd(N, K, seed=45)
+    ref = A.double() @ B.double().T
+    big = torch.full((4160, 2304), 7.0, device="cuda")
+    st = L.call("hif4x_gemm_tc", 0, 1, M, N, K, L.f32(1.0), L.ptr(A), K, L.ptr(B), K, L.f32(0.0), L.ptr(big), 2304,
+                L.stream())
+    assert st == L.OK
+    big2 = torch.full((M, 2305), 7.0, device="cuda")
+    st = L.call("hif4x_gemm_tc", 0, 1, M, N, K, L.f32(1.0), L.ptr(A), K, L.ptr(B), K, L.f32(0.0),
+                L.ptr(big2[:, 1:]), 2305, L.stream())
+    assert st == L.OK
+    assert L.lib().hif4x_device_status(L.stream()) == L.OK
+    for out, pad in ((big[:M, :N], [big[M:, :], big[:, N:]]), (big2[:, 1:N + 1], [big2[:, :1], big2[:, N + 1:]])):
+        assert float((out.double() - ref).abs().max() / ref.abs().max()) < 2e-6 * K ** 0.5 + 1e-6
+        for p in pad:
+            assert float((p - 7.0).abs().max()) == 0.0
+    assert torch.equal(big[:M, :N], big2[:, 1:N + 1])

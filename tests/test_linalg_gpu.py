@@ -265,11 +265,12 @@ def test_gptq_production_size_vs_oracle(capsys):
     assert abs(og / ow - 1) < 0.01
 
 
-@pytest.mark.parametrize("T,C", [(50, 70), (700, 1000), (2048, 4160), (1, 33)])
+@pytest.mark.parametrize("T,C", [(50, 70), (700, 1000), (2048, 4160), (1, 33), (520, 4200)])
 def test_gram_symmetric_vs_fp64(T, C):
     """hif4x_gram: the lower tiles (tensor cores from 2^26 multiply-adds on,
-    SIMT below) mirrored onto the upper triangle -- exactly symmetric, within
-    the fp32-GEMM bound of X^T X, and accumulating into a given matrix."""
+    SIMT below; 128 x 256 tiles along the diagonal for (520, 4200)) mirrored
+    onto the upper triangle -- exactly symmetric, within the fp32-GEMM bound
+    of X^T X, and accumulating into a given matrix."""
     X = rnd(T, C, seed=T + C)
     G = la.gram(X)
     assert torch.equal(G, G.T)
