@@ -496,6 +496,7 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
 
     packed, outputs, shards = {}, {}, {}
     compact_api = [False]
+    conv_ms = []   # this rank's host wall time of each device-resident conversion (before the gather)
 
     def step(device_resident: bool):
         if device_resident:
@@ -507,9 +508,11 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
             top = shard.matrix_cost(order[0].N, order[0].C, T_cal) if order else 0.0
             urgent = {j.key for j in order if shard.matrix_cost(j.N, j.C, T_cal) >= 0.5 * top}
             # each matrix packed on its worker's stream as it finishes; its dict5 and states are dropped
+            t_conv = time.perf_counter()
             done = weightset.convert(todo, workers=workers, device=dev, urgent=urgent,
                                      consume=lambda key, res, dyn: (shard.pack_params(res["weight_params"]),
                                                                     codec.pack(dyn)))
+            conv_ms.append((time.perf_counter() - t_conv) * 1e3)
             for key, (buf, dyn) in done.items():
                 packed[key] = buf
                 outputs[key] = dyn
@@ -560,6 +563,14 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
 
     dt = timed(True)
     clk.stop()
+    # every rank's step and conversion times (the step ends with the gather, so
+    # rank 0's step includes waiting for the slowest rank)
+    mine_t = {"step_ms": [round(x, 1) for x in window["step_ms"]],
+              "convert_ms": [round(x, 1) for x in conv_ms[-steps:]] if steps else []}
+    by_rank = [mine_t]
+    if dist is not None:
+        by_rank = [None] * ws
+        dist.all_gather_object(by_rank, mine_t)
     dev_packed = dict(packed)   # the device-resident run's weights, for the quality below
     digest = shard.checksum(shards) if rank == 0 else None
     gathered = len(shards)
@@ -594,7 +605,7 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
     return {
         "value": len(jobs) / dt, "unit": "matrices/s", "weight_gelem_per_s": elems / dt / 1e9,
         "n_gpus": ws, "steps": steps, "warmup": warmup, "ms_per_step": dt * 1e3,
-        "step_ms_rank0": window["step_ms"], "scaling": "strong", "matrices": len(jobs),
+        "step_ms_rank0": window["step_ms"], "ranks": by_rank, "scaling": "strong", "matrices": len(jobs),
         "weight_elements": elems, "clocks": clk.summary(*window["w"]),
         "gathered_bytes": int(sum(int(b.numel()) for b in shards.values())),
         "packed_checksum": digest,
