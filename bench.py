@@ -317,8 +317,11 @@ def run_gpu(args, rank, ws, local_rank):
     if not args.no_pipeline:
         del codes, e4m3, meta, hcodes, rt
         torch.cuda.empty_cache()
+        # each rank converts 1/N of the set per step, so its allocator pools take
+        # more steps to reach their steady size: 3 warm-ups at N = 1, 2 more per added rank
+        pw = args.pipeline_warmup if args.pipeline_warmup is not None else min(17, 3 + 2 * (ws - 1))
         pipeline = weightset_bench(rank, ws, local_rank, args.pipeline_layers, 8192, 4, 1024, args.pipeline_steps,
-                                   args.pipeline_warmup, args.workers)
+                                   pw, args.workers)
     if rank != 0:
         return
     elems = ROWS * COLS
@@ -952,9 +955,11 @@ def main():
     ap.add_argument("--pipeline-layers", type=int, default=32,
                     help="codec workload: decoder layers of the weight-set object (32 = the full weight set)")
     ap.add_argument("--pipeline-steps", type=int, default=2, help="timed conversions of the weight set")
-    ap.add_argument("--pipeline-warmup", type=int, default=3,
-                    help="untimed conversions of the weight set first (the first ones after start-up still "
-                         "grow the allocator's pools: 443, 86, 29, then 2-9 device allocations per conversion)")
+    ap.add_argument("--pipeline-warmup", type=int, default=None,
+                    help="untimed conversions of the weight set first (default 3 + 2 (N - 1), at most 17: the "
+                         "first ones after start-up still grow the allocator's pools, 443, 86, 29, then 2-9 "
+                         "device allocations per conversion on one GPU, and a rank converting 1/N of the set "
+                         "takes more conversions to get there)")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "codec":
         args.warmup = 3
