@@ -13,9 +13,10 @@
 // made the conversion's loads/stores and the MMA operand reads compete for
 // the shared-memory banks and capped the tensor pipe near 40 %.
 //
-// Persistent kernel, one CTA per SM (all but kTcFreeSms of them), 128 x 128 output tiles visited in
-// bands of GROUP tile-rows (column by column within a band) so that the CTAs
-// running at one time share A and B panels in L2.  192 threads:
+// Persistent kernel, one CTA per SM (all but kTcFreeSms of them), 128 x 128
+// or 128 x 256 output tiles (Tile<BN_>, chosen per call) visited in bands of
+// GROUP tile-rows (column by column within a band) so that the CTAs running
+// at one time share A and B panels in L2.  192 threads:
 //   warp 0   TMA producer (one lane) + tensor-memory allocation (whole warp)
 //   warp 1   MMA issuer (one lane): 4 K-substeps x 3 products per stage
 //   warps 2-5 epilogue: tcgen05.ld of their TMEM lane quarter -> alpha/beta

@@ -3,10 +3,11 @@
 //   * damped Cholesky -> upper factor of the inverse (GPTQ's Hinv)
 //   * GPTQ column-sequential quantize-and-propagate inside a column block
 //
-// The GEMM is a register-tiled SIMT kernel (128x128x8 CTA tile, 8x8 per
-// thread, double-buffered shared memory), fp32 in and out with fp32
-// accumulation, so every product matches the reference's fp32 matmuls to
-// rounding.
+// Products of at least 2^26 multiply-adds go to the tensor-core GEMM
+// (gemm_tc.cu, 3xTF32); smaller ones, and the products whose results are
+// differenced (hif4x_gemm_simt), run the register-tiled SIMT kernels here
+// (128x128x8 CTA tile with 8x8 per thread, or 32x32 tiles for small
+// products), fp32 in and out with sequential fp32 FMA accumulation.
 #include <algorithm>
 #include <cstdlib>
 #include <map>
