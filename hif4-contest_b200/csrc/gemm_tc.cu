@@ -817,11 +817,17 @@ int gemm_split(const float *As, int a_products, const float *Bs, int b_products,
                 N <= INT32_MAX && make_map_c(&mc, C, N, M, ldc))
                    ? 1
                    : 0;
-  static std::once_flag attr_once;
-  std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<128>::SMEM_BYTES);
-    cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<256>::SMEM_BYTES);
+  // the shared-memory opt-in is a property of the kernel in each device's context: once per device
+  static std::once_flag attr_once[kMaxDevices];
+  static bool attr_ok[kMaxDevices];
+  if (dev >= kMaxDevices) return HIF4X_ERR_UNSUPPORTED;
+  std::call_once(attr_once[dev], [dev] {
+    attr_ok[dev] = cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Tile<128>::SMEM_BYTES) == cudaSuccess &&
+                   cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Tile<256>::SMEM_BYTES) == cudaSuccess;
   });
+  if (!attr_ok[dev]) return HIF4X_ERR_LAUNCH;
   // leave kTcFreeSms SMs to the latency-bound kernels of other streams (the
   // Cholesky leaves and GPTQ column blocks of the same or another
   // calibration): a persistent grid on every SM holds them off until it ends

@@ -572,8 +572,17 @@ __global__ void __launch_bounds__(LTHREADS, 1) potrf_inv128_kernel(float *A, int
 static int potrf_inv128(float *A, int64_t ld, int b, float *Linv, int64_t ldi, int *info, int mode,
                         cudaStream_t s) {
   const int smem = (int)((2 * PB * LDS + LP * LDT) * sizeof(float));
-  if (cudaFuncSetAttribute(potrf_inv128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return HIF4X_ERR_LAUNCH;
+  // the shared-memory opt-in, once per device (a Cholesky calls this for every 128-row leaf)
+  constexpr int kDevs = 64;
+  static std::once_flag attr_once[kDevs];
+  static bool attr_ok[kDevs];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevs) return HIF4X_ERR_LAUNCH;
+  std::call_once(attr_once[dev], [dev, smem] {
+    attr_ok[dev] = cudaFuncSetAttribute(potrf_inv128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
+                   cudaSuccess;
+  });
+  if (!attr_ok[dev]) return HIF4X_ERR_LAUNCH;
   potrf_inv128_kernel<<<1, LTHREADS, smem, s>>>(A, ld, b, Linv, ldi, info, mode);
   HIF4X_CHECK_LAUNCH();
   return HIF4X_OK;
