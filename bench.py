@@ -453,7 +453,7 @@ def e2e_leg(args, K, codes, e4m3, s_dec, meta, hcodes, dev, stream, barrier, dis
 
 
 def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, warmup, workers,
-                    api_legs=False):
+                    api_legs=False, act_helper=True):
     """Pipeline workload: `layers` Llama-3-8B-shaped decoder layers (7 matrices
     each), full calibration (smoothing, rotation choice, GPTQ, refinement,
     Gram carries) plus one T_test-token dynamic activation call per matrix.
@@ -462,10 +462,14 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
     rank 0 by NCCL point-to-point inside the timed step.  Inputs are generated
     on the device (N(0, 0.02) weights; T_cal calibration tokens per layer
     input in n_cal samples, 0.2 % of the channels x20, the down_proj input
-    |N|*SiLU-shaped).  Returns the measurements on rank 0, None elsewhere."""
+    |N|*SiLU-shaped).  When LPT leaves a rank without matrices (one layer on
+    eight GPUs), that rank computes the costliest matrix's activation-side
+    factor for both transform modes and sends its owner the one it asks for
+    (hif4x.remote; off with act_helper=False).  Returns the measurements on
+    rank 0, None elsewhere."""
     import torch
 
-    from hif4x import codec, linear, score, shard, synth, weightset
+    from hif4x import codec, linear, remote, score, shard, synth, weightset
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     dist = None
@@ -473,6 +477,14 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
         import torch.distributed as dist
     jobs = shard.model_jobs(layers)
     mine = shard.rank_jobs(jobs, rank, ws, T_cal)
+    plan = shard.act_helper_plan(jobs, ws, T_cal) if (dist is not None and act_helper) else None
+    links, serve_job, serve_owner = {}, None, None
+    if plan is not None:
+        hj = jobs[plan[0]]
+        if rank == plan[1]:
+            links[hj.key] = remote.ActFactorLink(dist, plan[2], hj.C, dev)
+        elif rank == plan[2]:
+            serve_job, serve_owner = hj, plan[1]
 
     def pair(x):
         return list(synth.reference_form(*synth.quantize_nvfp4(x)))
@@ -484,7 +496,7 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
         return synth.acts_outlier(seed, T, C, n_out=max(1, round(C * 0.002)), gain=20.0, device=dev)
 
     dev_inputs, dev_weights = {}, {}
-    for j in mine:
+    for j in mine + ([serve_job] if serve_job is not None else []):
         key = (j.layer, j.input_id)
         if key not in dev_inputs:
             dev_inputs[key] = ([pair(acts(j.layer, j.input_id, j.C, i, T_cal // n_cal)) for i in range(n_cal)],
@@ -512,7 +524,12 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
             urgent = {j.key for j in order if shard.matrix_cost(j.N, j.C, T_cal) >= 0.5 * top}
             # each matrix packed on its worker's stream as it finishes; its dict5 and states are dropped
             t_conv = time.perf_counter()
-            done = weightset.convert(todo, workers=workers, device=dev, urgent=urgent,
+            if serve_job is not None:   # the owner's activation-side factor, both modes, then its request
+                wq, wsc = dev_weights[serve_job.key]
+                factors = linear.act_factors(wq, wsc, dev_inputs[(serve_job.layer, serve_job.input_id)][0])
+                remote.serve_act_factors(dist, serve_owner, factors, dev)
+                del factors
+            done = weightset.convert(todo, workers=workers, device=dev, urgent=urgent, links=links,
                                      consume=lambda key, res, dyn: (shard.pack_params(res["weight_params"]),
                                                                     codec.pack(dyn)))
             conv_ms.append((time.perf_counter() - t_conv) * 1e3)
@@ -609,6 +626,7 @@ def weightset_bench(rank, ws, local_rank, layers, T_cal, n_cal, T_test, steps, w
         "value": len(jobs) / dt, "unit": "matrices/s", "weight_gelem_per_s": elems / dt / 1e9,
         "n_gpus": ws, "steps": steps, "warmup": warmup, "ms_per_step": dt * 1e3,
         "step_ms_rank0": window["step_ms"], "ranks": by_rank, "scaling": "strong", "matrices": len(jobs),
+        "act_helper": None if plan is None else {"matrix": jobs[plan[0]].key, "owner": plan[1], "helper": plan[2]},
         "weight_elements": elems, "clocks": clk.summary(*window["w"]),
         "gathered_bytes": int(sum(int(b.numel()) for b in shards.values())),
         "packed_checksum": digest,
@@ -679,10 +697,14 @@ def run_matrix(args, rank, ws, local_rank):
     4 samples (8192 as the weight-set object, 4096 as the layer workload) and
     one 1024-token dynamic call, with
     the calibration's phase times from CUDA events (linear.calibrate_weight's
-    info).  A profiling and latency workload: every rank runs its own copy."""
+    info).  A profiling and latency workload: every rank runs its own copy.
+    --act-factor-given: the activation-side factor is handed to the
+    calibration ready-made (linear.act_factors, computed before each step and
+    outside its timing), the owner's critical path when another GPU computes
+    that factor (hif4x.remote); add its NVLink transfer, C x C fp32."""
     import torch
 
-    from hif4x import linear, shard, synth
+    from hif4x import linear, remote, shard, synth
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     N, C, input_id = shard.LLAMA3_8B_LAYER[args.matrix]
@@ -702,9 +724,17 @@ def run_matrix(args, rank, ws, local_rank):
     wpair = pair((torch.randn(N, C, device=dev, generator=g) * 0.02).to(torch.bfloat16))
     torch.cuda.synchronize(dev)
 
+    given = {}
+
+    def prepare():
+        if args.act_factor_given:
+            given["f"] = linear.act_factors(wpair[0], wpair[1], calib)
+            torch.cuda.synchronize(dev)
+
     def step(info=None):
+        link = remote.LocalActFactors(given["f"]) if args.act_factor_given else None
         res = linear.calibrate_weight(wpair[0], wpair[1], calib, info=info, return_device=True,
-                                      rng=torch.Generator().manual_seed(0))
+                                      rng=torch.Generator().manual_seed(0), act_link=link)
         linear.dynamic_activation(test[0], test[1], res["activation_state"], return_device=True)
         return res
 
@@ -712,24 +742,29 @@ def run_matrix(args, rank, ws, local_rank):
     clk.start()
 
     for _ in range(args.warmup):
+        prepare()
         step()
     torch.cuda.synchronize(dev)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    step_ms = []
     w0 = time.time()
-    evs[0].record()
     for k in range(args.steps):
+        prepare()   # untimed: the factor another GPU would have computed meanwhile
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         step()
-        evs[k + 1].record()
-    torch.cuda.synchronize(dev)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        step_ms.append(e0.elapsed_time(e1))
     win = (w0, time.time())
     clk.stop()
-    step_ms = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
     info = {}
+    prepare()
     step(info)
     if rank != 0:
         return
     print(json.dumps({
         "metric": f"one {args.matrix} calibration + one dynamic call, ms", "value": statistics.median(step_ms),
+        "act_factor_given": bool(args.act_factor_given),
         "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "step_ms": step_ms, "clocks": clk.summary(*win),
         "phases_ms": info.get("phases_ms"), "decisions": {k: info.get(k) for k in ("alpha", "mode", "gptq_w",
@@ -828,7 +863,7 @@ def run_gemm(args, rank, ws, local_rank):
 def run_layer(args, rank, ws, local_rank):
     """--workload layer: the weight-set pipeline alone, with the API legs."""
     res = weightset_bench(rank, ws, local_rank, args.layers, 4096, 4, 1024, args.steps, args.warmup, args.workers,
-                          api_legs=not args.no_e2e)
+                          api_legs=not args.no_e2e, act_helper=not args.no_act_helper)
     if rank != 0:
         return
     api = res.pop("api")
@@ -952,6 +987,10 @@ def main():
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
     ap.add_argument("--workers", type=int, default=6, help="weight sets: matrices in flight per GPU")
     ap.add_argument("--no-pipeline", action="store_true", help="codec workload: skip the weight-set object")
+    ap.add_argument("--act-factor-given", action="store_true",
+                    help="matrix workload: the activation-side factor computed beforehand, outside the timing")
+    ap.add_argument("--no-act-helper", action="store_true",
+                    help="layer workload: no idle rank computes the longest matrix's activation-side factor")
     ap.add_argument("--pipeline-layers", type=int, default=32,
                     help="codec workload: decoder layers of the weight-set object (32 = the full weight set)")
     ap.add_argument("--pipeline-steps", type=int, default=2, help="timed conversions of the weight set")

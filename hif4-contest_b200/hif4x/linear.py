@@ -236,32 +236,17 @@ def _refine_weight_values(w_final, q_used, weight_params: Dict5, calib_sm, mode)
     return weight_params, q_used
 
 
-def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, calib_activation_list: list,
-                     info: dict | None = None, return_device: bool = False,
-                     rng: torch.Generator | None = None, compact: bool = False,
-                     shared: SharedFactors | None = None) -> dict[str, Any]:
-    """hif4_calibration_and_quantize_weight (solution.py:826-1026).
-
-    return_device=True keeps the weight parameters and the state tensors on the
-    GPU (for device-resident pipelines); the API form returns CPU tensors.
-    rng: a CPU generator seeded 0 to draw the subsampling permutations from
-    instead of re-seeding the global one (the same values; lets calibrations
-    run concurrently from several threads).
-    compact=True writes the compact activation state (compact_state): the
-    dynamic call rebuilds u_act / gw / gwf on the device, bit for bit.
-    shared: a SharedFactors of the weight set this matrix belongs to (the
-    transform-choice factor is then computed once per calibration list and
-    alpha); the results are the same."""
-    if rng is None:
-        torch.manual_seed(0)                                   # solution.py:838
-    dev = _dev()
-    ph = _Phases(info is not None)
-    ph.mark("start")
+def _smoothed(weight_quant: torch.Tensor, weight_scale: torch.Tensor, calib_activation_list: list, dev,
+              rng: torch.Generator | None, ph: "_Phases | None" = None):
+    """Decode, the alpha smoothing search and the smoothed operands
+    (solution.py:839-873).  Returns (w, w_abs, s, best_alpha, w_s, acts_s);
+    w_abs is the refinement gate's hash, launched, not read."""
     w = decode_pair((weight_quant, weight_scale), dev)
     R, C = w.shape
     acts_raw = [decode_pair(p, dev) for p in calib_activation_list]
     w_abs = la.abs_sum_async(w)          # the refinement gate's hash (read after the act-side guard)
-    ph.mark("upload_decode")
+    if ph is not None:
+        ph.mark("upload_decode")
 
     # ---- alpha smoothing search (solution.py:844-873)
     abs_sum = torch.zeros(C, dtype=torch.float32, device=dev)
@@ -291,6 +276,74 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     w_s = la.scale_cols(w, s, L.SMOOTH_DIV)
     acts_s = [la.scale_cols(a, s, L.SMOOTH_MUL) for a in acts_raw]
     del acts_raw
+    return w, w_abs, s, best_alpha, w_s, acts_s
+
+
+def act_factors(weight_quant: torch.Tensor, weight_scale: torch.Tensor, calib_activation_list: list,
+                modes=(0, 1), rng: torch.Generator | None = None) -> dict:
+    """The activation-side factor calibrate_weight uses when its weight guard
+    keeps the searched encode (solution.py:936-951), for each transform mode
+    in `modes` (at most two, computed on two streams): {mode: (Ua, order)}
+    with the act order (None after the reference's fallback to the unpermuted
+    factorisation; Ua None when that fails too), or {} when the calibration
+    has no activation-side step.  The same alpha search and values as
+    calibrate_weight with a generator seeded 0, so the factor is the one the
+    calibration would compute -- another GPU can compute it while the
+    calibration runs its transform choice and weight GPTQ (act_link)."""
+    if rng is None:
+        rng = torch.Generator().manual_seed(0)
+    dev = _dev()
+    w, _, _, _, w_s, acts_s = _smoothed(weight_quant, weight_scale, calib_activation_list, dev, rng)
+    R, C = w.shape
+    if not (R > 64 and len(acts_s) >= 2 and acts_s[-1].shape[0] >= 8):   # calibrate_weight's xh_pick gate
+        return {}
+    main = torch.cuda.current_stream(dev)
+    side = _side_stream(dev)
+    side.wait_stream(main)
+    specs = {}
+    for m, stream in zip(modes, (main, side)):
+        with torch.cuda.stream(stream):
+            specs[m] = _act_factor_launch(_search(tf(w_s, m))[1])
+    main.wait_stream(side)
+    infos = la.read_scalars(*(c.info for _, _, c in specs.values()))
+    out = {}
+    for (m, (Ha, order, chol)), info in zip(specs.items(), infos):
+        chol.U.record_stream(main)
+        order.record_stream(main)
+        chol.release()
+        out[m] = (chol.U, order) if info == 0 else (la.chol_upper_inv(Ha), None)
+    return out
+
+
+def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, calib_activation_list: list,
+                     info: dict | None = None, return_device: bool = False,
+                     rng: torch.Generator | None = None, compact: bool = False,
+                     shared: SharedFactors | None = None, act_link=None) -> dict[str, Any]:
+    """hif4_calibration_and_quantize_weight (solution.py:826-1026).
+
+    return_device=True keeps the weight parameters and the state tensors on the
+    GPU (for device-resident pipelines); the API form returns CPU tensors.
+    rng: a CPU generator seeded 0 to draw the subsampling permutations from
+    instead of re-seeding the global one (the same values; lets calibrations
+    run concurrently from several threads).
+    compact=True writes the compact activation state (compact_state): the
+    dynamic call rebuilds u_act / gw / gwf on the device, bit for bit.
+    shared: a SharedFactors of the weight set this matrix belongs to (the
+    transform-choice factor is then computed once per calibration list and
+    alpha); the results are the same.
+    act_link: a source of the activation-side factor computed elsewhere
+    (act_factors on another GPU, hif4x.remote.ActFactorLink): when the weight
+    guard keeps the searched encode, fetch(mode) returns (Ua, order) and the
+    factorisation is not run here; otherwise decline() is called and it runs
+    here.  Every calibration calls exactly one of the two.  The results are
+    the same."""
+    if rng is None:
+        torch.manual_seed(0)                                   # solution.py:838
+    dev = _dev()
+    ph = _Phases(info is not None)
+    ph.mark("start")
+    w, w_abs, s, best_alpha, w_s, acts_s = _smoothed(weight_quant, weight_scale, calib_activation_list, dev, rng, ph)
+    R, C = w.shape
     ph.mark("alpha_search")
 
     # ---- transform choice {0: none, 1: rotation} (solution.py:875-911)
@@ -366,7 +419,7 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     # through q_used: start it for the searched encode on the side stream while
     # the weight GPTQ runs, and redo it below only if GPTQ wins
     spec = None
-    if xh_pick is not None:
+    if xh_pick is not None and act_link is None:
         main = torch.cuda.current_stream(dev)
         side = _side_stream(dev)
         side.wait_stream(main)
@@ -393,15 +446,25 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
     # ---- activation-side GPTQ with act-order (solution.py:936-976)
     u_act, gptq_act, order = None, 0, None
     w_abs_v = None
+    if xh_pick is None and act_link is not None:
+        act_link.decline()
     if xh_pick is not None:
         main = torch.cuda.current_stream(dev)
         main.wait_stream(_side_stream(dev))
-        if spec is None or gptq_w:
-            spec = _act_factor_launch(q_used)
-        Ha, order_p, chol = spec
+        chol = remote = None
+        if act_link is not None and not gptq_w:
+            # the factor of the searched encode's values, computed elsewhere
+            # (the reference's non-positive-pivot fallback already applied)
+            remote = act_link.fetch(mode)
+        else:
+            if act_link is not None:
+                act_link.decline()
+            if spec is None or gptq_w:
+                spec = _act_factor_launch(q_used)
+            Ha, order_p, chol = spec
+            chol.U.record_stream(main)
+            order_p.record_stream(main)
         spec = None
-        chol.U.record_stream(main)
-        order_p.record_stream(main)
         p_r, xr, unit_x = _search(xh_pick)
         # x' @ q^T - xh @ w^T = (x' - xh) @ q^T + xh @ (q - w)^T
         if res_q is None:
@@ -417,17 +480,22 @@ def calibrate_weight(weight_quant: torch.Tensor, weight_scale: torch.Tensor, cal
                 xg = la.gptq(xh_pick, unit_x, Ua)
             return la.sq_sum_async(la.gemm(la.sub(xg, xh_pick), q_used, tb=True, beta=1.0, out=res_q.clone()))
 
-        # the permuted factor is used before its pivot flag is read: the flag,
-        # both losses and the refinement gate's hash come back in one read
-        sq_ag = act_gptq_sq(chol.U, order_p)
-        info_a, sq_ar_v, sq_ag_v, w_abs_v = la.read_scalars(chol.info, la.sq_sum_async(r_ar), sq_ag, w_abs)
-        chol.release()
-        Ua, order = chol.U, order_p
-        if info_a != 0:
-            # a non-positive pivot: the reference's fallback, the unpermuted factorisation
-            Ua, order = la.chol_upper_inv(Ha), None
+        if chol is not None:
+            # the permuted factor is used before its pivot flag is read: the flag,
+            # both losses and the refinement gate's hash come back in one read
+            sq_ag = act_gptq_sq(chol.U, order_p)
+            info_a, sq_ar_v, sq_ag_v, w_abs_v = la.read_scalars(chol.info, la.sq_sum_async(r_ar), sq_ag, w_abs)
+            chol.release()
+            Ua, order = chol.U, order_p
+            if info_a != 0:
+                # a non-positive pivot: the reference's fallback, the unpermuted factorisation
+                Ua, order = la.chol_upper_inv(Ha), None
+                if Ua is not None:
+                    sq_ag_v = la.read_scalars(act_gptq_sq(Ua, None))[0]
+        else:
+            Ua, order = remote
             if Ua is not None:
-                sq_ag_v = la.read_scalars(act_gptq_sq(Ua, None))[0]
+                sq_ar_v, sq_ag_v, w_abs_v = la.read_scalars(la.sq_sum_async(r_ar), act_gptq_sq(Ua, order), w_abs)
         if Ua is not None and sq_ag_v / n_act < sq_ar_v / n_act:
             u_act = Ua
             gptq_act = 1

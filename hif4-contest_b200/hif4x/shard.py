@@ -62,6 +62,20 @@ def lpt_assign(costs: list[float], world: int) -> list[int]:
     return owner
 
 
+def act_helper_plan(jobs: list[MatrixJob], world: int, T_cal: int):
+    """(index of the costliest job, its rank, a rank with no job) when LPT
+    leaves a rank without work (fewer matrices than ranks, e.g. one layer on
+    eight GPUs), else None: that rank computes the costliest matrix's
+    activation-side factor for its owner (hif4x.remote)."""
+    costs = [matrix_cost(j.N, j.C, T_cal) for j in jobs]
+    owner = lpt_assign(costs, world)
+    idle = sorted(set(range(world)) - set(owner))
+    if not jobs or not idle:
+        return None
+    top = max(range(len(jobs)), key=lambda i: (costs[i], -i))
+    return top, owner[top], idle[0]
+
+
 def rank_jobs(jobs: list[MatrixJob], rank: int, world: int, T_cal: int) -> list[MatrixJob]:
     owner = lpt_assign([matrix_cost(j.N, j.C, T_cal) for j in jobs], world)
     return [j for j, o in zip(jobs, owner) if o == rank]

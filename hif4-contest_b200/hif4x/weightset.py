@@ -29,7 +29,7 @@ def _worker_stream(dev, i: int, urgent: bool = False) -> torch.cuda.Stream:
     return _STREAMS[key]
 
 
-def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None) -> dict:
+def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None, links=None) -> dict:
     """jobs: [(key, weight_pair, calib_pairs, test_pair or None)], pairs as
     the six-function API takes them (CPU or CUDA tensors).  Returns
     {key: (calibration result, dynamic result or None)} with every tensor left
@@ -45,7 +45,9 @@ def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None
     GPTQ column blocks, one CTA each) do not queue behind the many-CTA
     kernels of the shorter matrices beside it.  Matrices whose jobs hold the
     same calibration list object share their transform-choice factor when
-    they pick the same smoothing exponent (linear.SharedFactors)."""
+    they pick the same smoothing exponent (linear.SharedFactors).  links:
+    {key: act_link} for matrices whose activation-side factor another GPU
+    computes (hif4x.remote.ActFactorLink; linear.calibrate_weight)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     users: dict = {}
     for job in jobs:
@@ -69,7 +71,8 @@ def convert(jobs: list, workers: int = 2, device=None, consume=None, urgent=None
             with torch.cuda.stream(_worker_stream(dev, i, key in urgent)):
                 try:
                     res = linear.calibrate_weight(wpair[0], wpair[1], calib, return_device=True,
-                                                  rng=torch.Generator().manual_seed(0), shared=shared)
+                                                  rng=torch.Generator().manual_seed(0), shared=shared,
+                                                  act_link=(links or {}).get(key))
                     dyn = None
                     if test is not None:
                         dyn = linear.dynamic_activation(test[0], test[1], res["activation_state"],
