@@ -111,7 +111,7 @@ def main():
 
     # ---------------- codec: decode / rotation / encode / alg1 --------------
     out = {}
-    # NVFP4 decode (A1): BASELINE-style weight, packed and reference forms
+    # NVFP4 decode (A1): a Llama-style weight, packed and reference forms
     w = synth.weight_c0(11, 64, 512)
     codes, e4m3, s_dec = synth.quantize_nvfp4(w)
     carrier, scale = synth.reference_form(codes, e4m3, s_dec)
