@@ -776,6 +776,37 @@ def run_matrix(args, rank, ws, local_rank):
     }), flush=True)
 
 
+def cupti_kernel_list(fn, dev, top: int = 12) -> dict:
+    """fn() once under torch.profiler's CUDA activity (CUPTI kernel records,
+    no replay): per kernel its launches, total device time and share of the
+    summed kernel time, and the call's span.  Concurrent kernels (side
+    streams) overlap, so the shares are of summed, not elapsed, time."""
+    import collections
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize(dev)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize(dev)
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    t0 = t1 = None
+    for e in prof.events():
+        if e.device_type != torch.autograd.DeviceType.CUDA or e.name.startswith(("Memcpy", "Memset")):
+            continue
+        nm = e.name.split("(")[0].replace("void ", "")
+        agg[nm][0] += 1
+        agg[nm][1] += e.time_range.elapsed_us()
+        t0 = e.time_range.start if t0 is None else min(t0, e.time_range.start)
+        t1 = e.time_range.end if t1 is None else max(t1, e.time_range.end)
+    tot = sum(v[1] for v in agg.values()) or 1.0
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])[:top]
+    return {"span_ms": round((t1 - t0) / 1e3, 3) if t0 is not None else 0.0,
+            "kernel_ms_sum": round(tot / 1e3, 3),
+            "kernels": [{"name": n, "launches": c, "ms": round(t / 1e3, 3), "share": round(t / tot, 4)}
+                        for n, (c, t) in rows]}
+
+
 def run_gemm(args, rank, ws, local_rank):
     """--workload gemm: the tensor-core products of the calibration timed
     alone with CUDA events and a clock record -- the lower-tile Gram of a
@@ -846,6 +877,8 @@ def run_gemm(args, rank, ws, local_rank):
         tfs = flops / (ms * 1e-3) / 1e12
         out[name] = {"ms": ms, "fp32_equiv_tflops": tfs, "roofline_tflops": bf16 / 6, "frac": tfs / (bf16 / 6),
                      "clocks": clk.summary(w0, w1)}
+        if args.kernel_list:   # one more call under CUPTI (torch.profiler): its kernels, counts and shares
+            out[name]["kernel_list"] = cupti_kernel_list(fn, dev)
         if name in hbm_bytes:   # memory-bound: HBM roofline on the algorithmic bytes
             gbs = hbm_bytes[name] / (ms * 1e-3) / 1e9
             out[name].update({"bound": "hbm", "alg_bytes": hbm_bytes[name], "achieved_gbs": gbs,
@@ -982,6 +1015,8 @@ def main():
     ap.add_argument("--workload", default="codec", choices=["codec", "layer", "attention", "matrix", "gemm"])
     ap.add_argument("--matrix", default="down_proj", help="matrix workload: Llama-3-8B layer matrix name")
     ap.add_argument("--case", default="", help="gemm workload: run only the cases whose name contains this")
+    ap.add_argument("--kernel-list", action="store_true",
+                    help="gemm workload: one more call of each case under CUPTI, its kernels and their shares")
     ap.add_argument("--tokens", type=int, default=8192,
                     help="matrix workload: calibration tokens (4 samples; 8192 as the weight set, 4096 as one layer)")
     ap.add_argument("--layers", type=int, default=1, help="layer workload: decoder layers")
